@@ -1,0 +1,77 @@
+/*
+ * kb200.h -- C ABI of the B200 (sm_100a) implementation of the Kairos
+ * hybrid-attention hot path.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t
+ * (passed as void*), launches asynchronously on that stream, never
+ * synchronises the host, and returns 0 on success or a KB200_ERR_* code.
+ * kb200_last_error() returns a human-readable message for the last failure
+ * on the calling thread.  No entry point allocates device memory: callers
+ * pass any scratch they need as a workspace pointer sized by the matching
+ * *_workspace_size() query.
+ *
+ * Layouts follow the reference's PyTorch operators ("head-last", contiguous):
+ *   q, k  [B*T, H, K]  bf16        v  [B*T, H, V] bf16
+ *   g     [B*T, H]     fp32 (log-space decay)   beta [B*T, H] bf16
+ *   states [N, H, K, V] fp32
+ */
+#ifndef KB200_H
+#define KB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  KB200_OK = 0,
+  KB200_ERR_INVALID = 1,     /* bad shape / null pointer / unsupported dims   */
+  KB200_ERR_ALIGN = 2,       /* pointer not 16-byte aligned                   */
+  KB200_ERR_WORKSPACE = 3,   /* workspace missing or too small                */
+  KB200_ERR_LAUNCH = 4,      /* CUDA launch error                             */
+  KB200_ERR_TIMEOUT = 5      /* a bounded device-side wait gave up            */
+};
+
+/* ABI version; bumped on any signature change. */
+int kb200_abi_version(void);
+/* Message for the last error returned on this thread ("" if none). */
+const char* kb200_last_error(void);
+
+/* ---------------------------------------------------------------------
+ * Gated delta rule, chunked forward (chunk size 64).
+ * Replaces chunk_gated_delta_rule / chunk_gated_delta_rule_fwd:
+ *   kairos/third_party/fla/ops/gated_delta_rule/chunk.py:216-323 (public op)
+ *   kairos/third_party/fla/ops/gated_delta_rule/chunk.py:16-67  (pipeline)
+ * with use_qk_l2norm_in_kernel handled in-kernel (chunk.py:166-168).
+ * --------------------------------------------------------------------- */
+typedef struct KB200GdnArgs {
+  const void* q;            /* [B*T, H, K] bf16                                 */
+  const void* k;            /* [B*T, H, K] bf16                                 */
+  const void* v;            /* [B*T, H, V] bf16                                 */
+  const float* g;           /* [B*T, H] fp32 log decay                          */
+  const void* beta;         /* [B*T, H] bf16                                    */
+  const float* initial_state; /* [N, H, K, V] fp32 or NULL                      */
+  void* o;                  /* out [B*T, H, V] bf16                             */
+  float* final_state;       /* out [N, H, K, V] fp32 or NULL                    */
+  const int32_t* cu_seqlens;  /* device [N+1] or NULL (then N = B, length T)    */
+  const int32_t* chunk_indices; /* device [num_chunks, 2] (seq, chunk) or NULL  */
+  const int32_t* chunk_offsets; /* device [N+1] first chunk of each seq or NULL */
+  int64_t B, T, H, K, V;    /* T = tokens per sequence (B*T = total tokens)     */
+  int64_t N;                /* number of sequences (B, or len(cu_seqlens)-1)    */
+  int64_t num_chunks;       /* total 64-token chunks over all sequences         */
+  float scale;              /* output scale (reference default K^-1/2)          */
+  int use_qk_l2norm;        /* 1: L2-normalise q and k inside the op            */
+} KB200GdnArgs;
+
+/* Bytes of workspace kb200_gdn_chunk_fwd needs for these arguments. */
+size_t kb200_gdn_workspace_size(const KB200GdnArgs* a);
+/* Launch the forward.  `workspace` must be 256-byte aligned. */
+int kb200_gdn_chunk_fwd(const KB200GdnArgs* a, void* workspace, size_t workspace_bytes,
+                        void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KB200_H */

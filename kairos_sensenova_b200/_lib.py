@@ -1,0 +1,70 @@
+"""ctypes binding of ``libkb200.so`` (declarations in ``include/kb200.h``).
+
+The library is the product's only compute path.  If it is missing or fails
+to load, :func:`lib` raises -- there is no CPU or eager fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+_LIB_PATH = Path(__file__).resolve().parent / 'libkb200.so'
+_lock = threading.Lock()
+_lib = None
+
+KB200_OK = 0
+ERRORS = {1: 'invalid argument', 2: 'misaligned pointer', 3: 'workspace', 4: 'launch failure',
+          5: 'device wait timed out'}
+
+
+class GdnArgs(ctypes.Structure):
+    """Mirror of ``KB200GdnArgs`` (include/kb200.h)."""
+    _fields_ = [
+        ('q', ctypes.c_void_p), ('k', ctypes.c_void_p), ('v', ctypes.c_void_p),
+        ('g', ctypes.c_void_p), ('beta', ctypes.c_void_p), ('initial_state', ctypes.c_void_p),
+        ('o', ctypes.c_void_p), ('final_state', ctypes.c_void_p),
+        ('cu_seqlens', ctypes.c_void_p), ('chunk_indices', ctypes.c_void_p),
+        ('chunk_offsets', ctypes.c_void_p),
+        ('B', ctypes.c_int64), ('T', ctypes.c_int64), ('H', ctypes.c_int64),
+        ('K', ctypes.c_int64), ('V', ctypes.c_int64), ('N', ctypes.c_int64),
+        ('num_chunks', ctypes.c_int64), ('scale', ctypes.c_float), ('use_qk_l2norm', ctypes.c_int),
+    ]
+
+
+# name -> (restype, argtypes); every symbol include/kb200.h declares
+SIGNATURES = {
+    'kb200_abi_version': (ctypes.c_int, []),
+    'kb200_last_error': (ctypes.c_char_p, []),
+    'kb200_gdn_workspace_size': (ctypes.c_size_t, [ctypes.POINTER(GdnArgs)]),
+    'kb200_gdn_chunk_fwd': (ctypes.c_int, [ctypes.POINTER(GdnArgs), ctypes.c_void_p,
+                                           ctypes.c_size_t, ctypes.c_void_p]),
+}
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not _LIB_PATH.exists():
+                raise RuntimeError(
+                    f'{_LIB_PATH} is missing: build it with `python -m kairos_sensenova_b200.build` '
+                    '(there is no fallback implementation)')
+            handle = ctypes.CDLL(str(_LIB_PATH))
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(handle, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = handle
+    return _lib
+
+
+def check(rc: int, what: str) -> None:
+    if rc != KB200_OK:
+        msg = lib().kb200_last_error().decode(errors='replace')
+        kind = ERRORS.get(rc, f'error {rc}')
+        if rc == 1:
+            raise ValueError(f'{what}: {msg}')
+        raise RuntimeError(f'{what} failed ({kind}): {msg}')

@@ -1,0 +1,743 @@
+// gdn_chunk.cu -- chunked gated delta rule forward for sm_100a.
+//
+// Three launches per call (chunk size BT = 64):
+//   1. gdn_prepare_kernel  (parallel over chunks x heads)
+//        optional L2-norm of q,k  (fla/modules/l2norm.py:98-130)
+//        in-chunk gate cumsum      (fla/ops/utils/cumsum.py:27-65)
+//        A = beta e^{g_i-g_j} K K^T, strictly lower  (fla/ops/common/chunk_scaled_dot_kkt.py:28-73)
+//        Ai = (I + A)^-1           (fla/ops/utils/solve_tril.py:184-331)
+//        u = Ai (beta v), w = Ai (beta e^g k)   (fla/ops/gated_delta_rule/wy_fast.py:27-81)
+//   2. gdn_state_kernel    (sequential over chunks; parallel over heads x V-slices)
+//        h snapshot, v_new = u - w h, gate, h <- e^{g_last} h + k^T v_new
+//        (fla/ops/common/chunk_delta_h.py:52-224)
+//   3. gdn_output_kernel   (parallel over chunks x heads x V-slices)
+//        o = scale (e^g (q h) + tril(q k^T e^{g_i-g_j}) v_new)   (fla/ops/common/chunk_o.py:41-128)
+//
+// Numerics follow the reference's bf16 rounding points: normalised q/k, Ai,
+// w, u, h snapshots and v_new are bf16; A, the cumsum, the state and all
+// accumulations are fp32.  Tensor-core work uses mma.sync m16n8k16 bf16.
+#include "common.cuh"
+#include "kb200_internal.h"
+
+namespace kb {
+namespace gdn {
+
+constexpr int BT = 64;
+constexpr int NTHREADS = 128;
+
+struct Params {
+  const __nv_bfloat16* q;
+  const __nv_bfloat16* k;
+  const __nv_bfloat16* v;
+  const float* g;
+  const __nv_bfloat16* beta;
+  const float* h0;
+  __nv_bfloat16* o;
+  float* ht;
+  const int32_t* cu_seqlens;
+  const int32_t* chunk_indices;
+  const int32_t* chunk_offsets;
+  // workspace
+  __nv_bfloat16* qn;  // normalised q (or == q)
+  __nv_bfloat16* kn;  // normalised k (or == k)
+  float* gc;          // in-chunk cumsum of g
+  __nv_bfloat16* w;
+  __nv_bfloat16* u;
+  __nv_bfloat16* vnew;
+  __nv_bfloat16* hs;  // [num_chunks, H, K, V] state snapshots
+  int T, H, NT;       // NT = chunks per sequence when cu_seqlens == nullptr
+  float scale;
+  int l2norm;
+};
+
+// Locate chunk `c` (global index): sequence n, first token bos, in-sequence chunk it, length L.
+struct ChunkLoc { int n, it, bos, len; };
+KB_DEVI ChunkLoc locate_chunk(const Params& p, int c) {
+  ChunkLoc r;
+  if (p.cu_seqlens) {
+    r.n = p.chunk_indices[2 * c];
+    r.it = p.chunk_indices[2 * c + 1];
+    int s = p.cu_seqlens[r.n], e = p.cu_seqlens[r.n + 1];
+    r.bos = s;
+    r.len = min(BT, e - s - r.it * BT);
+  } else {
+    r.n = c / p.NT;
+    r.it = c % p.NT;
+    r.bos = r.n * p.T;
+    r.len = min(BT, p.T - r.it * BT);
+  }
+  return r;
+}
+
+// ---------------------------------------------------------------------------
+// Kernel 1: per-chunk preparation.
+// ---------------------------------------------------------------------------
+template <int K, int V>
+struct PrepSmem {
+  static constexpr int LDK = K + 8, LDV = V + 8, LDA = BT + 1, LDI = BT + 8;
+  __nv_bfloat16 ks[BT * LDK];   // k (normalised) then reused for beta e^g k
+  __nv_bfloat16 vb[BT * LDV];   // beta v
+  __nv_bfloat16 ai[BT * LDI];   // (I+A)^-1 in bf16
+  float af[BT * LDA];           // A (strictly lower), fp32
+  float xf[BT * LDA];           // (I+A)^-1, fp32
+  float yf[16 * 48];            // block-merge temporaries
+  float gcs[BT];
+  float bs[BT];
+};
+
+template <int K, int V>
+__global__ void __launch_bounds__(NTHREADS) gdn_prepare_kernel(Params p) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  using S = PrepSmem<K, V>;
+  S& sm = *reinterpret_cast<S*>(smem_raw);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int c = blockIdx.x, h = blockIdx.y, H = p.H;
+  const ChunkLoc loc = locate_chunk(p, c);
+  const int t0 = loc.bos + loc.it * BT, L = loc.len;
+
+  // ---- q/k rows: optional L2 norm (one warp per row), k kept in smem ----
+  constexpr int EPL = K / 32;  // elements per lane
+  for (int r = warp; r < BT; r += NTHREADS / 32) {
+    __nv_bfloat16* dst = sm.ks + r * S::LDK + lane * EPL;
+    if (r < L) {
+      const size_t off = ((size_t)(t0 + r) * H + h) * K + lane * EPL;
+      float x[EPL];
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) x[e] = __bfloat162float(p.k[off + e]);
+      if (p.l2norm) {
+        float ss = 0.f;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) ss += x[e] * x[e];
+        ss = warp_sum(ss);
+        const float rstd = 1.0f / sqrtf(ss + 1e-6f);
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) {
+          __nv_bfloat16 y = __float2bfloat16_rn(x[e] * rstd);
+          dst[e] = y;
+          p.kn[off + e] = y;
+        }
+        // q: same normalisation, written to the workspace for the output kernel
+        float y2[EPL];
+        float sq = 0.f;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) { y2[e] = __bfloat162float(p.q[off + e]); sq += y2[e] * y2[e]; }
+        sq = warp_sum(sq);
+        const float rq = 1.0f / sqrtf(sq + 1e-6f);
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) p.qn[off + e] = __float2bfloat16_rn(y2[e] * rq);
+      } else {
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) dst[e] = p.k[off + e];
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) dst[e] = __float2bfloat16_rn(0.f);
+    }
+  }
+  // ---- gate cumsum (warp 0) and beta ----
+  if (warp == 0) {
+    const int i0 = 2 * lane, i1 = 2 * lane + 1;
+    float g0 = (i0 < L) ? p.g[(size_t)(t0 + i0) * H + h] : 0.f;
+    float g1 = (i1 < L) ? p.g[(size_t)(t0 + i1) * H + h] : 0.f;
+    float pair = g0 + g1, incl = pair;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      float y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    const float excl = incl - pair;
+    const float c0 = excl + g0, c1 = excl + g0 + g1;
+    sm.gcs[i0] = c0;
+    sm.gcs[i1] = c1;
+    if (i0 < L) p.gc[(size_t)(t0 + i0) * H + h] = c0;
+    if (i1 < L) p.gc[(size_t)(t0 + i1) * H + h] = c1;
+  } else if (warp == 1) {
+    for (int i = lane; i < BT; i += 32)
+      sm.bs[i] = (i < L) ? __bfloat162float(p.beta[(size_t)(t0 + i) * H + h]) : 0.f;
+  }
+  // ---- beta v rows (bf16(v * beta)) ----
+  __syncthreads();
+  {
+    constexpr int VPR = V / 8;  // 16-byte vectors per row
+    for (int idx = tid; idx < BT * VPR; idx += NTHREADS) {
+      const int r = idx / VPR, cv = (idx % VPR) * 8;
+      uint4 raw = make_uint4(0, 0, 0, 0);
+      if (r < L) raw = *reinterpret_cast<const uint4*>(p.v + ((size_t)(t0 + r) * H + h) * V + cv);
+      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
+      const float b = sm.bs[r];
+      uint4 outv;
+      uint32_t* ov = reinterpret_cast<uint32_t*>(&outv);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        ov[j] = pack_bf16(__bfloat162float(e[2 * j]) * b, __bfloat162float(e[2 * j + 1]) * b);
+      *reinterpret_cast<uint4*>(sm.vb + r * S::LDV + cv) = outv;
+    }
+  }
+  // ---- A = beta_i e^{g_i - g_j} <k_i, k_j>, strictly lower (warp w: rows 16w..16w+15) ----
+  {
+    float acc[8][4];
+#pragma unroll
+    for (int n = 0; n < 8; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[n][e] = 0.f;
+#pragma unroll 4
+    for (int kk = 0; kk < K; kk += 16) {
+      uint32_t a[4];
+      load_a_rowmajor(a, sm.ks, S::LDK, warp * 16, kk, lane);
+#pragma unroll
+      for (int n0 = 0; n0 < BT; n0 += 16) {
+        uint32_t b[4];
+        load_b_nmajor_rows_x2n(b, sm.ks, S::LDK, kk, n0, lane);
+        mma_bf16(acc[n0 / 8], a, b);
+        mma_bf16(acc[n0 / 8 + 1], a, b + 2);
+      }
+    }
+    const int g8 = lane >> 2, t4 = lane & 3;
+#pragma unroll
+    for (int n = 0; n < 8; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = warp * 16 + g8 + ((e >> 1) << 3);
+        const int j = n * 8 + 2 * t4 + (e & 1);
+        float val = 0.f;
+        if (i > j && i < L) val = acc[n][e] * __expf(sm.gcs[i] - sm.gcs[j]) * sm.bs[i];
+        sm.af[i * S::LDA + j] = val;
+      }
+  }
+  __syncthreads();
+  // ---- k rows -> bf16(bf16(k * beta) * e^{g}) in place (wy_fast.py:77-79) ----
+  {
+    constexpr int VPR = K / 8;
+    for (int idx = tid; idx < BT * VPR; idx += NTHREADS) {
+      const int r = idx / VPR, cv = (idx % VPR) * 8;
+      __nv_bfloat16* row = sm.ks + r * S::LDK + cv;
+      uint4 raw = *reinterpret_cast<uint4*>(row);
+      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
+      const float b = sm.bs[r], eg = __expf(sm.gcs[r]);
+      uint4 outv;
+      uint32_t* ov = reinterpret_cast<uint32_t*>(&outv);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        ov[j] = pack_bf16(bf16_round(__bfloat162float(e[2 * j]) * b) * eg,
+                          bf16_round(__bfloat162float(e[2 * j + 1]) * b) * eg);
+      *reinterpret_cast<uint4*>(row) = outv;
+    }
+  }
+  // ---- (I + A)^-1: 16x16 diagonal blocks by forward substitution ----
+  if (tid < 64) {
+    const int blk = tid >> 4, col = tid & 15, base = blk * 16;
+    float x[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) x[r] = (r == col) ? 1.f : 0.f;
+#pragma unroll
+    for (int r = 1; r < 16; ++r) {
+      float s = 0.f;
+#pragma unroll
+      for (int m = 0; m < r; ++m) s += sm.af[(base + r) * S::LDA + base + m] * x[m];
+      if (r > col) x[r] = -s;
+    }
+#pragma unroll
+    for (int r = 0; r < 16; ++r) sm.xf[(base + r) * S::LDA + base + col] = x[r];
+  }
+  // zero the strictly-upper blocks
+  for (int idx = tid; idx < BT * BT; idx += NTHREADS) {
+    const int r = idx >> 6, cc = idx & 63;
+    if ((cc >> 4) > (r >> 4)) sm.xf[r * S::LDA + cc] = 0.f;
+  }
+  __syncthreads();
+  // ---- block merge: X_ij = -D_i sum_{m=j}^{i-1} A_im X_mj, block rows in order ----
+  for (int bi = 1; bi < 4; ++bi) {
+    const int ncols = bi * 16;  // columns j-blocks 0..bi-1
+    for (int idx = tid; idx < 16 * ncols; idx += NTHREADS) {
+      const int r = idx / ncols, cc = idx % ncols;
+      const int jb = cc >> 4;
+      float s = 0.f;
+      for (int m = jb * 16; m < bi * 16; ++m)
+        s += sm.af[(bi * 16 + r) * S::LDA + m] * sm.xf[m * S::LDA + cc];
+      sm.yf[r * 48 + cc] = s;
+    }
+    __syncthreads();
+    for (int idx = tid; idx < 16 * ncols; idx += NTHREADS) {
+      const int r = idx / ncols, cc = idx % ncols;
+      float s = 0.f;
+      for (int m = 0; m <= r; ++m)
+        s += sm.xf[(bi * 16 + r) * S::LDA + bi * 16 + m] * sm.yf[m * 48 + cc];
+      sm.xf[(bi * 16 + r) * S::LDA + cc] = -s;
+    }
+    __syncthreads();
+  }
+  for (int idx = tid; idx < BT * BT; idx += NTHREADS) {
+    const int r = idx >> 6, cc = idx & 63;
+    sm.ai[r * S::LDI + cc] = __float2bfloat16_rn(sm.xf[r * S::LDA + cc]);
+  }
+  __syncthreads();
+  // ---- u = Ai (beta v), w = Ai (beta e^g k), 64-column slabs ----
+  {
+    const int g8 = lane >> 2, t4 = lane & 3;
+    uint32_t afr[4][4];
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) load_a_rowmajor(afr[ks], sm.ai, S::LDI, warp * 16, ks * 16, lane);
+    const int r0 = warp * 16 + g8, r1 = r0 + 8;
+    for (int slab = 0; slab < (V + K) / 64; ++slab) {
+      const bool isu = slab < V / 64;
+      const __nv_bfloat16* src = isu ? sm.vb : sm.ks;
+      const int ld = isu ? S::LDV : S::LDK;
+      const int c0 = (isu ? slab : slab - V / 64) * 64;
+      float acc[8][4];
+#pragma unroll
+      for (int n = 0; n < 8; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[n][e] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+#pragma unroll
+        for (int n0 = 0; n0 < 64; n0 += 16) {
+          uint32_t b[4];
+          load_b_kmajor_rows_x2n(b, src, ld, ks * 16, c0 + n0, lane);
+          mma_bf16(acc[n0 / 8], afr[ks], b);
+          mma_bf16(acc[n0 / 8 + 1], afr[ks], b + 2);
+        }
+      __nv_bfloat16* dst = isu ? p.u : p.w;
+      const int D = isu ? V : K;
+#pragma unroll
+      for (int n = 0; n < 8; ++n) {
+        const int col = c0 + n * 8 + 2 * t4;
+        if (r0 < L)
+          *reinterpret_cast<uint32_t*>(dst + ((size_t)(t0 + r0) * H + h) * D + col) =
+              pack_bf16(acc[n][0], acc[n][1]);
+        if (r1 < L)
+          *reinterpret_cast<uint32_t*>(dst + ((size_t)(t0 + r1) * H + h) * D + col) =
+              pack_bf16(acc[n][2], acc[n][3]);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Kernel 2: sequential state pass.  Grid (V / BV, N * H); 4 warps.
+// Warp w owns state rows [w*K/4, (w+1)*K/4) x BV columns in fp32 registers.
+// Per chunk: w, k, u tiles are double-buffered in shared memory (cp.async).
+// ---------------------------------------------------------------------------
+template <int K, int BV>
+struct StateSmem {
+  static constexpr int LDK = K + 8, LDV = BV + 8;
+  __nv_bfloat16 ws[2][BT * LDK];
+  __nv_bfloat16 ks[2][BT * LDK];
+  __nv_bfloat16 us[2][BT * LDV];
+  __nv_bfloat16 hb[K * LDV];      // bf16 snapshot of the state (B operand of w h)
+  __nv_bfloat16 vg[BT * LDV];     // gated v_new (B operand of k^T v)
+  float gcs[2][BT];
+};
+
+template <int K, int BV>
+KB_DEVI void state_issue_loads(StateSmem<K, BV>& sm, int buf, const Params& p, int t0, int L,
+                               int h, int v0, int V, int tid) {
+  const int H = p.H;
+  constexpr int KV = K / 8, VV = BV / 8;
+  for (int idx = tid; idx < BT * KV; idx += NTHREADS) {
+    const int r = idx / KV, cv = (idx % KV) * 8;
+    const bool ok = r < L;
+    const size_t off = ((size_t)(t0 + (ok ? r : 0)) * H + h) * K + cv;
+    cp_async16(&sm.ws[buf][r * StateSmem<K, BV>::LDK + cv], p.w + off, ok);
+    cp_async16(&sm.ks[buf][r * StateSmem<K, BV>::LDK + cv], p.kn + off, ok);
+  }
+  for (int idx = tid; idx < BT * VV; idx += NTHREADS) {
+    const int r = idx / VV, cv = (idx % VV) * 8;
+    const bool ok = r < L;
+    const size_t off = ((size_t)(t0 + (ok ? r : 0)) * H + h) * V + v0 + cv;
+    cp_async16(&sm.us[buf][r * StateSmem<K, BV>::LDV + cv], p.u + off, ok);
+  }
+  if (tid < BT) sm.gcs[buf][tid] = (tid < L) ? p.gc[(size_t)(t0 + tid) * H + h] : 0.f;
+  cp_async_commit();
+}
+
+template <int K, int V, int BV>
+__global__ void __launch_bounds__(NTHREADS) gdn_state_kernel(Params p) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  using S = StateSmem<K, BV>;
+  S& sm = *reinterpret_cast<S*>(smem_raw);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g8 = lane >> 2, t4 = lane & 3;
+  const int v0 = blockIdx.x * BV;
+  const int nh = blockIdx.y, n = nh / p.H, h = nh % p.H, H = p.H;
+  int bos, Tn, cbase;
+  if (p.cu_seqlens) {
+    bos = p.cu_seqlens[n];
+    Tn = p.cu_seqlens[n + 1] - bos;
+    cbase = p.chunk_offsets[n];
+  } else {
+    bos = n * p.T;
+    Tn = p.T;
+    cbase = n * p.NT;
+  }
+  const int NTn = (Tn + BT - 1) / BT;
+  constexpr int RW = K / 4;        // state rows per warp
+  constexpr int MT = RW / 16;      // m-tiles per warp
+  constexpr int NB = BV / 8;       // n-tiles
+  float hacc[MT][NB][4];
+#pragma unroll
+  for (int m = 0; m < MT; ++m)
+#pragma unroll
+    for (int nn = 0; nn < NB; ++nn)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = warp * RW + m * 16 + g8 + ((e >> 1) << 3);
+        const int cc = v0 + nn * 8 + 2 * t4 + (e & 1);
+        hacc[m][nn][e] = p.h0 ? p.h0[((size_t)nh * K + r) * V + cc] : 0.f;
+      }
+  if (NTn > 0) state_issue_loads<K, BV>(sm, 0, p, bos, min(BT, Tn), h, v0, V, tid);
+
+  for (int it = 0; it < NTn; ++it) {
+    const int buf = it & 1;
+    const int t0 = bos + it * BT, L = min(BT, Tn - it * BT);
+    // (a) snapshot: bf16 state -> smem operand and -> global h[chunk]
+    __nv_bfloat16* hg = p.hs + ((size_t)(cbase + it) * H + h) * K * V;
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+#pragma unroll
+      for (int nn = 0; nn < NB; ++nn) {
+        const int r = warp * RW + m * 16 + g8;
+        const int cc = nn * 8 + 2 * t4;
+        const uint32_t lo = pack_bf16(hacc[m][nn][0], hacc[m][nn][1]);
+        const uint32_t hi = pack_bf16(hacc[m][nn][2], hacc[m][nn][3]);
+        *reinterpret_cast<uint32_t*>(&sm.hb[r * S::LDV + cc]) = lo;
+        *reinterpret_cast<uint32_t*>(&sm.hb[(r + 8) * S::LDV + cc]) = hi;
+        *reinterpret_cast<uint32_t*>(hg + (size_t)r * V + v0 + cc) = lo;
+        *reinterpret_cast<uint32_t*>(hg + (size_t)(r + 8) * V + v0 + cc) = hi;
+      }
+    cp_async_wait<0>();
+    __syncthreads();
+    if (it + 1 < NTn)
+      state_issue_loads<K, BV>(sm, buf ^ 1, p, t0 + BT, min(BT, Tn - (it + 1) * BT), h, v0, V, tid);
+    // (b) v_new = u - w h   (warp w: rows 16w..16w+15)
+    const float glast = sm.gcs[buf][L - 1];
+    {
+      float acc[NB][4];
+#pragma unroll
+      for (int nn = 0; nn < NB; ++nn)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[nn][e] = 0.f;
+#pragma unroll 4
+      for (int kk = 0; kk < K; kk += 16) {
+        uint32_t a[4];
+        load_a_rowmajor(a, sm.ws[buf], S::LDK, warp * 16, kk, lane);
+#pragma unroll
+        for (int n0 = 0; n0 < BV; n0 += 16) {
+          uint32_t b[4];
+          load_b_kmajor_rows_x2n(b, sm.hb, S::LDV, kk, n0, lane);
+          mma_bf16(acc[n0 / 8], a, b);
+          mma_bf16(acc[n0 / 8 + 1], a, b + 2);
+        }
+      }
+      const int r0 = warp * 16 + g8, r1 = r0 + 8;
+      const float e0 = (r0 < L) ? __expf(glast - sm.gcs[buf][r0]) : 0.f;
+      const float e1 = (r1 < L) ? __expf(glast - sm.gcs[buf][r1]) : 0.f;
+#pragma unroll
+      for (int nn = 0; nn < NB; ++nn) {
+        const int cc = nn * 8 + 2 * t4;
+        const __nv_bfloat162 u0 = *reinterpret_cast<const __nv_bfloat162*>(&sm.us[buf][r0 * S::LDV + cc]);
+        const __nv_bfloat162 u1 = *reinterpret_cast<const __nv_bfloat162*>(&sm.us[buf][r1 * S::LDV + cc]);
+        const float a0 = __low2float(u0) - acc[nn][0], a1 = __high2float(u0) - acc[nn][1];
+        const float a2 = __low2float(u1) - acc[nn][2], a3 = __high2float(u1) - acc[nn][3];
+        if (r0 < L)
+          *reinterpret_cast<uint32_t*>(p.vnew + ((size_t)(t0 + r0) * H + h) * V + v0 + cc) = pack_bf16(a0, a1);
+        if (r1 < L)
+          *reinterpret_cast<uint32_t*>(p.vnew + ((size_t)(t0 + r1) * H + h) * V + v0 + cc) = pack_bf16(a2, a3);
+        *reinterpret_cast<uint32_t*>(&sm.vg[r0 * S::LDV + cc]) = pack_bf16(a0 * e0, a1 * e0);
+        *reinterpret_cast<uint32_t*>(&sm.vg[r1 * S::LDV + cc]) = pack_bf16(a2 * e1, a3 * e1);
+      }
+    }
+    __syncthreads();
+    // (c) h <- e^{g_last} h + k^T vg
+    {
+      const float dec = __expf(glast);
+#pragma unroll
+      for (int m = 0; m < MT; ++m)
+#pragma unroll
+        for (int nn = 0; nn < NB; ++nn)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) hacc[m][nn][e] *= dec;
+#pragma unroll
+      for (int kk = 0; kk < BT; kk += 16) {
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+          uint32_t a[4];
+          load_a_transposed(a, sm.ks[buf], S::LDK, warp * RW + m * 16, kk, lane);
+#pragma unroll
+          for (int n0 = 0; n0 < BV; n0 += 16) {
+            uint32_t b[4];
+            load_b_kmajor_rows_x2n(b, sm.vg, S::LDV, kk, n0, lane);
+            mma_bf16(hacc[m][n0 / 8], a, b);
+            mma_bf16(hacc[m][n0 / 8 + 1], a, b + 2);
+          }
+        }
+      }
+    }
+    __syncthreads();
+  }
+  if (p.ht) {
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+#pragma unroll
+      for (int nn = 0; nn < NB; ++nn)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int r = warp * RW + m * 16 + g8 + ((e >> 1) << 3);
+          const int cc = v0 + nn * 8 + 2 * t4 + (e & 1);
+          p.ht[((size_t)nh * K + r) * V + cc] = hacc[m][nn][e];
+        }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Kernel 3: output.  Grid (V / BVO, num_chunks, H); 4 warps, warp w: rows 16w..16w+15.
+// ---------------------------------------------------------------------------
+template <int K, int BVO>
+struct OutSmem {
+  static constexpr int LDK = K + 8, LDV = BVO + 8;
+  __nv_bfloat16 qs[BT * LDK];
+  __nv_bfloat16 ks[BT * LDK];
+  __nv_bfloat16 hs[K * LDV];
+  __nv_bfloat16 vs[BT * LDV];
+  float gcs[BT];
+};
+
+template <int K, int V, int BVO>
+__global__ void __launch_bounds__(NTHREADS) gdn_output_kernel(Params p) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  using S = OutSmem<K, BVO>;
+  S& sm = *reinterpret_cast<S*>(smem_raw);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g8 = lane >> 2, t4 = lane & 3;
+  const int v0 = blockIdx.x * BVO, c = blockIdx.y, h = blockIdx.z, H = p.H;
+  const ChunkLoc loc = locate_chunk(p, c);
+  const int t0 = loc.bos + loc.it * BT, L = loc.len;
+  {
+    constexpr int KV = K / 8, VV = BVO / 8;
+    for (int idx = tid; idx < BT * KV; idx += NTHREADS) {
+      const int r = idx / KV, cv = (idx % KV) * 8;
+      const bool ok = r < L;
+      const size_t off = ((size_t)(t0 + (ok ? r : 0)) * H + h) * K + cv;
+      cp_async16(&sm.qs[r * S::LDK + cv], p.qn + off, ok);
+      cp_async16(&sm.ks[r * S::LDK + cv], p.kn + off, ok);
+    }
+    const __nv_bfloat16* hg = p.hs + ((size_t)c * H + h) * K * V + v0;
+    for (int idx = tid; idx < K * VV; idx += NTHREADS) {
+      const int r = idx / VV, cv = (idx % VV) * 8;
+      cp_async16(&sm.hs[r * S::LDV + cv], hg + (size_t)r * V + cv, true);
+    }
+    for (int idx = tid; idx < BT * VV; idx += NTHREADS) {
+      const int r = idx / VV, cv = (idx % VV) * 8;
+      const bool ok = r < L;
+      cp_async16(&sm.vs[r * S::LDV + cv], p.vnew + ((size_t)(t0 + (ok ? r : 0)) * H + h) * V + v0 + cv, ok);
+    }
+    cp_async_commit();
+    if (tid < BT) sm.gcs[tid] = (tid < L) ? p.gc[(size_t)(t0 + tid) * H + h] : 0.f;
+    cp_async_wait<0>();
+    __syncthreads();
+  }
+  constexpr int NB = BVO / 8;
+  float acc[NB][4];
+  float sa[8][4];
+#pragma unroll
+  for (int nn = 0; nn < NB; ++nn)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[nn][e] = 0.f;
+#pragma unroll
+  for (int nn = 0; nn < 8; ++nn)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) sa[nn][e] = 0.f;
+#pragma unroll 2
+  for (int kk = 0; kk < K; kk += 16) {
+    uint32_t a[4];
+    load_a_rowmajor(a, sm.qs, S::LDK, warp * 16, kk, lane);
+#pragma unroll
+    for (int n0 = 0; n0 < BVO; n0 += 16) {
+      uint32_t b[4];
+      load_b_kmajor_rows_x2n(b, sm.hs, S::LDV, kk, n0, lane);
+      mma_bf16(acc[n0 / 8], a, b);
+      mma_bf16(acc[n0 / 8 + 1], a, b + 2);
+    }
+#pragma unroll
+    for (int n0 = 0; n0 < BT; n0 += 16) {
+      uint32_t b[4];
+      load_b_nmajor_rows_x2n(b, sm.ks, S::LDK, kk, n0, lane);
+      mma_bf16(sa[n0 / 8], a, b);
+      mma_bf16(sa[n0 / 8 + 1], a, b + 2);
+    }
+  }
+  const int r0 = warp * 16 + g8, r1 = r0 + 8;
+  const float gr0 = sm.gcs[r0], gr1 = sm.gcs[r1];
+  const float eg0 = __expf(gr0), eg1 = __expf(gr1);
+#pragma unroll
+  for (int nn = 0; nn < NB; ++nn) {
+    acc[nn][0] *= eg0; acc[nn][1] *= eg0;
+    acc[nn][2] *= eg1; acc[nn][3] *= eg1;
+  }
+  // gated causal scores -> bf16 A fragments (C-fragment layout equals A-fragment layout pairwise)
+  uint32_t af[4][4];
+#pragma unroll
+  for (int nn = 0; nn < 8; ++nn) {
+    float x[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int i = (e < 2) ? r0 : r1;
+      const int j = nn * 8 + 2 * t4 + (e & 1);
+      x[e] = (j <= i && i < L) ? sa[nn][e] * __expf(sm.gcs[i] - sm.gcs[j]) : 0.f;
+    }
+    const int kstep = nn >> 1, hi = nn & 1;
+    af[kstep][hi ? 2 : 0] = pack_bf16(x[0], x[1]);
+    af[kstep][hi ? 3 : 1] = pack_bf16(x[2], x[3]);
+  }
+#pragma unroll
+  for (int ks = 0; ks < 4; ++ks)
+#pragma unroll
+    for (int n0 = 0; n0 < BVO; n0 += 16) {
+      uint32_t b[4];
+      load_b_kmajor_rows_x2n(b, sm.vs, S::LDV, ks * 16, n0, lane);
+      mma_bf16(acc[n0 / 8], af[ks], b);
+      mma_bf16(acc[n0 / 8 + 1], af[ks], b + 2);
+    }
+  const float sc = p.scale;
+#pragma unroll
+  for (int nn = 0; nn < NB; ++nn) {
+    const int cc = v0 + nn * 8 + 2 * t4;
+    if (r0 < L)
+      *reinterpret_cast<uint32_t*>(p.o + ((size_t)(t0 + r0) * H + h) * V + cc) =
+          pack_bf16(acc[nn][0] * sc, acc[nn][1] * sc);
+    if (r1 < L)
+      *reinterpret_cast<uint32_t*>(p.o + ((size_t)(t0 + r1) * H + h) * V + cc) =
+          pack_bf16(acc[nn][2] * sc, acc[nn][3] * sc);
+  }
+}
+
+}  // namespace gdn
+}  // namespace kb
+
+// ===========================================================================
+// Host side: C ABI
+// ===========================================================================
+namespace {
+using namespace kb;
+
+struct WsLayout { size_t qn, kn, gc, w, u, vnew, hs, total; };
+
+WsLayout ws_layout(const KB200GdnArgs* a) {
+  const size_t TT = (size_t)a->B * a->T, H = a->H, K = a->K, V = a->V;
+  WsLayout L{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) { size_t o = off; off = align_up(off + bytes); return o; };
+  const size_t nqk = a->use_qk_l2norm ? TT * H * K * 2 : 0;
+  L.qn = take(nqk);
+  L.kn = take(nqk);
+  L.gc = take(TT * H * 4);
+  L.w = take(TT * H * K * 2);
+  L.u = take(TT * H * V * 2);
+  L.vnew = take(TT * H * V * 2);
+  L.hs = take((size_t)a->num_chunks * H * K * V * 2);
+  L.total = off;
+  return L;
+}
+
+int validate(const KB200GdnArgs* a) {
+  if (!a) return set_error(KB200_ERR_INVALID, "gdn: null args");
+  if (a->B <= 0 || a->T < 0 || a->H <= 0)
+    return set_error(KB200_ERR_INVALID, "gdn: bad shape B=%lld T=%lld H=%lld", (long long)a->B,
+                     (long long)a->T, (long long)a->H);
+  if (!((a->K == 128 || a->K == 256) && (a->V == 128 || a->V == 256 || a->V == 512)))
+    return set_error(KB200_ERR_INVALID, "gdn: unsupported head dims K=%lld V=%lld (K in {128,256}, V in {128,256,512})",
+                     (long long)a->K, (long long)a->V);
+  if (a->cu_seqlens && (a->B != 1 || !a->chunk_indices || !a->chunk_offsets))
+    return set_error(KB200_ERR_INVALID, "gdn: varlen needs B == 1 and chunk_indices/chunk_offsets");
+  if (!a->cu_seqlens) {
+    const int64_t nt = (a->T + 63) / 64;
+    if (a->N != a->B || a->num_chunks != a->B * nt)
+      return set_error(KB200_ERR_INVALID, "gdn: N must be B and num_chunks B*ceil(T/64)");
+  }
+  if ((a->B * a->T) * a->H * (a->K > a->V ? a->K : a->V) >= (int64_t)1 << 31)
+    return set_error(KB200_ERR_INVALID, "gdn: tensor too large for 32-bit token indexing");
+  const void* ptrs[] = {a->q, a->k, a->v, a->o};
+  for (const void* p : ptrs) {
+    if (!p) return set_error(KB200_ERR_INVALID, "gdn: null tensor pointer");
+    if (!aligned16(p)) return set_error(KB200_ERR_ALIGN, "gdn: q/k/v/o must be 16-byte aligned");
+  }
+  if (!a->g || !a->beta) return set_error(KB200_ERR_INVALID, "gdn: null g/beta");
+  return KB200_OK;
+}
+
+template <int K, int V>
+int launch(const KB200GdnArgs* a, const WsLayout& L, char* ws, cudaStream_t st) {
+  gdn::Params p{};
+  p.q = (const __nv_bfloat16*)a->q;
+  p.k = (const __nv_bfloat16*)a->k;
+  p.v = (const __nv_bfloat16*)a->v;
+  p.g = a->g;
+  p.beta = (const __nv_bfloat16*)a->beta;
+  p.h0 = a->initial_state;
+  p.o = (__nv_bfloat16*)a->o;
+  p.ht = a->final_state;
+  p.cu_seqlens = a->cu_seqlens;
+  p.chunk_indices = a->chunk_indices;
+  p.chunk_offsets = a->chunk_offsets;
+  p.qn = a->use_qk_l2norm ? (__nv_bfloat16*)(ws + L.qn) : (__nv_bfloat16*)a->q;
+  p.kn = a->use_qk_l2norm ? (__nv_bfloat16*)(ws + L.kn) : (__nv_bfloat16*)a->k;
+  p.gc = (float*)(ws + L.gc);
+  p.w = (__nv_bfloat16*)(ws + L.w);
+  p.u = (__nv_bfloat16*)(ws + L.u);
+  p.vnew = (__nv_bfloat16*)(ws + L.vnew);
+  p.hs = (__nv_bfloat16*)(ws + L.hs);
+  p.T = (int)a->T;
+  p.H = (int)a->H;
+  p.NT = (int)((a->T + 63) / 64);
+  p.scale = a->scale;
+  p.l2norm = a->use_qk_l2norm;
+  const int H = (int)a->H;
+  const int nchunks = (int)a->num_chunks;
+  constexpr int BV = 32, BVO = 64;
+  if (nchunks > 0) {
+    const size_t s1 = sizeof(gdn::PrepSmem<K, V>);
+    cudaFuncSetAttribute(gdn::gdn_prepare_kernel<K, V>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s1);
+    gdn::gdn_prepare_kernel<K, V><<<dim3(nchunks, H), gdn::NTHREADS, s1, st>>>(p);
+    if (int e = check_launch("gdn_prepare_kernel")) return e;
+  }
+  const size_t s2 = sizeof(gdn::StateSmem<K, BV>);
+  cudaFuncSetAttribute(gdn::gdn_state_kernel<K, V, BV>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s2);
+  gdn::gdn_state_kernel<K, V, BV><<<dim3(V / BV, (unsigned)(a->N * H)), gdn::NTHREADS, s2, st>>>(p);
+  if (int e = check_launch("gdn_state_kernel")) return e;
+  if (nchunks > 0) {
+    const size_t s3 = sizeof(gdn::OutSmem<K, BVO>);
+    cudaFuncSetAttribute(gdn::gdn_output_kernel<K, V, BVO>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s3);
+    gdn::gdn_output_kernel<K, V, BVO><<<dim3(V / BVO, nchunks, H), gdn::NTHREADS, s3, st>>>(p);
+    if (int e = check_launch("gdn_output_kernel")) return e;
+  }
+  return KB200_OK;
+}
+}  // namespace
+
+extern "C" size_t kb200_gdn_workspace_size(const KB200GdnArgs* a) {
+  if (validate(a) != KB200_OK) return 0;
+  return ws_layout(a).total;
+}
+
+extern "C" int kb200_gdn_chunk_fwd(const KB200GdnArgs* a, void* workspace, size_t workspace_bytes,
+                                   void* stream) {
+  if (int e = validate(a)) return e;
+  const WsLayout L = ws_layout(a);
+  if (!workspace || workspace_bytes < L.total)
+    return kb::set_error(KB200_ERR_WORKSPACE, "gdn: workspace needs %zu bytes, got %zu", L.total,
+                         workspace_bytes);
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return kb::set_error(KB200_ERR_ALIGN, "gdn: workspace must be 256-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+#define KB_GDN_CASE(KK, VV) \
+  if (a->K == KK && a->V == VV) return launch<KK, VV>(a, L, ws, st);
+  KB_GDN_CASE(128, 128)
+  KB_GDN_CASE(128, 256)
+  KB_GDN_CASE(128, 512)
+  KB_GDN_CASE(256, 128)
+  KB_GDN_CASE(256, 256)
+  KB_GDN_CASE(256, 512)
+#undef KB_GDN_CASE
+  return kb::set_error(KB200_ERR_INVALID, "gdn: unsupported dims");
+}

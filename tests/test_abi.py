@@ -1,0 +1,66 @@
+"""C-ABI library: loads, exports every symbol include/kb200.h declares, and
+rejects bad arguments without touching a GPU (the validators run on the host)."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from kairos_sensenova_b200 import _lib
+
+HEADER = Path(__file__).resolve().parent.parent / 'include' / 'kb200.h'
+
+
+def declared_symbols():
+    return sorted(set(re.findall(r'\b(kb200_[a-z0-9_]+)\s*\(', HEADER.read_text())))
+
+
+def test_library_loads_and_exports_all_declared_symbols():
+    L = _lib.lib()
+    syms = declared_symbols()
+    assert 'kb200_gdn_chunk_fwd' in syms
+    for s in syms:
+        assert hasattr(L, s), s
+        assert s in _lib.SIGNATURES, f'{s} has no ctypes signature'
+
+
+def test_abi_version():
+    assert _lib.lib().kb200_abi_version() == 1
+
+
+def _args(**kw):
+    base = dict(q=16, k=16, v=16, g=16, beta=16, o=16, B=1, T=100, H=2, K=128, V=128, N=1,
+                num_chunks=2, scale=1.0, use_qk_l2norm=1)
+    base.update(kw)
+    return _lib.GdnArgs(**base)
+
+
+def test_gdn_workspace_size_and_validation():
+    L = _lib.lib()
+    a = _args()
+    n = L.kb200_gdn_workspace_size(ctypes.byref(a))
+    # gc + w + u + v_new + h snapshots + normalised q,k
+    TT, H, K, V = 100, 2, 128, 128
+    assert n >= TT * H * (4 + 2 * K * 2 + 2 * K + 2 * V * 2) + 2 * H * K * V * 2
+    for bad in (dict(K=96), dict(V=64), dict(num_chunks=3), dict(B=0)):
+        assert L.kb200_gdn_workspace_size(ctypes.byref(_args(**bad))) == 0
+    rc = L.kb200_gdn_chunk_fwd(ctypes.byref(_args(K=96)), None, 0, None)
+    assert rc == 1 and b'unsupported head dims' in L.kb200_last_error()
+    rc = L.kb200_gdn_chunk_fwd(ctypes.byref(_args(q=8)), None, 0, None)
+    assert rc == 2
+    rc = L.kb200_gdn_chunk_fwd(ctypes.byref(_args()), None, 0, None)
+    assert rc == 3 and b'workspace' in L.kb200_last_error()
+
+
+def test_python_op_rejects_cpu_and_grad():
+    import torch
+    from kairos_sensenova_b200 import chunk_gated_delta_rule
+    q = torch.zeros(1, 4, 1, 128)
+    with pytest.raises(RuntimeError, match='CUDA'):
+        chunk_gated_delta_rule(q, q, q, q[..., 0], q[..., 0])
+    with pytest.raises(ValueError, match='batch size'):
+        chunk_gated_delta_rule(torch.zeros(2, 4, 1, 128), q, q, q[..., 0], q[..., 0],
+                               cu_seqlens=torch.tensor([0, 4]))
+    qg = q.clone().requires_grad_()
+    with pytest.raises(NotImplementedError):
+        chunk_gated_delta_rule(qg, q, q, q[..., 0], q[..., 0])
