@@ -71,6 +71,24 @@ size_t kb200_gdn_workspace_size(const KB200GdnArgs* a);
 int kb200_gdn_chunk_fwd(const KB200GdnArgs* a, void* workspace, size_t workspace_bytes,
                         void* stream);
 
+/* ---------------------------------------------------------------------
+ * Softmax attention with FP8-e4m3 Q/K/V, per-(batch, head) amax scaling
+ * (scale = amax/448), fp32 softmax and accumulation, bf16 output.
+ * Replaces the attention core called by AttentionModule.forward
+ *   kairos/modules/dits/kairos_dit.py:367-373 (module)
+ *   kairos/modules/dits/kairos_dit.py:232-277 (flash_attention dispatcher;
+ *   non-causal, no mask, softmax scale D^-1/2 as in F.scaled_dot_product_attention)
+ * q, k, v, o: [B, S, H*D] bf16, D = 128.
+ * two_term = 1 adds a second e4m3 term (the rounding residual, same per-head
+ * scale) to q and to v, which doubles the tensor-core work and lifts the
+ * cosine similarity to the bf16 reference from ~0.9986 to ~0.9993 on
+ * N(0,1) inputs; two_term = 0 is the plain single-term e4m3 path.
+ * --------------------------------------------------------------------- */
+size_t kb200_attn_fp8_workspace_size(int64_t B, int64_t S, int64_t H, int64_t D, int two_term);
+int kb200_attn_fp8_fwd(const void* q, const void* k, const void* v, void* o, int64_t B, int64_t S,
+                       int64_t H, int64_t D, float softmax_scale, int two_term, void* workspace,
+                       size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,71 @@
+"""FP8 attention module with the reference's ``AttentionModule`` interface.
+
+``AttentionModule(num_heads).forward(q, k, v, attn_mask=None, window_size=(-1, -1))``
+with q, k, v ``[B, S, N*D]`` bf16 returns ``[B, S, N*D]`` bf16
+(``kairos/modules/dits/kairos_dit.py:362-373``).  The core is computed by the
+sm_100a kernels behind ``kb200_attn_fp8_fwd``: per-(batch, head) amax scaling
+of q/k/v to e4m3, non-causal softmax(q k^T / sqrt(D)) v with fp32 softmax and
+accumulation.  By default q and v carry a second e4m3 term (the rounding
+residual at the same per-head scale): a single e4m3 term bounds the cosine
+similarity to the bf16 reference near 0.9986 on N(0,1) data, below the 0.999
+contract, and the residual term lifts it to ~0.9993.  Like the reference's
+quantised backends (``SageAttention3Module``, ``kairos_dit.py:398-420``) it
+raises ``NotImplementedError`` for an ``attn_mask``; it also raises for a
+sliding ``window_size``, which it does not implement.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+
+from . import _lib
+
+
+def attention_fp8(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, num_heads: int,
+                  softmax_scale: float | None = None, two_term: bool = True) -> torch.Tensor:
+    """q, k, v: [B, S, H*D] (bf16; other float dtypes are converted) -> [B, S, H*D] bf16."""
+    if q.device.type != 'cuda':
+        raise RuntimeError('attention_fp8: inputs must be CUDA tensors (no CPU path)')
+    if q.dim() != 3 or k.shape != q.shape or v.shape != q.shape:
+        raise ValueError(f'attention_fp8: q/k/v must share shape [B,S,H*D], got {tuple(q.shape)}, '
+                         f'{tuple(k.shape)}, {tuple(v.shape)}')
+    B, S, HD = q.shape
+    if HD % num_heads:
+        raise ValueError(f'attention_fp8: hidden {HD} not divisible by num_heads {num_heads}')
+    D = HD // num_heads
+    if softmax_scale is None:
+        softmax_scale = D ** -0.5
+    dev = q.device
+    with torch.cuda.device(dev):
+        qc, kc, vc = (x.to(torch.bfloat16).contiguous() for x in (q, k, v))
+        o = torch.empty_like(qc)
+        L = _lib.lib()
+        nbytes = L.kb200_attn_fp8_workspace_size(B, S, num_heads, D, int(two_term))
+        if nbytes == 0:
+            raise ValueError(f'attention_fp8: unsupported shape B={B} S={S} H={num_heads} D={D} (D must be 128)')
+        ws = torch.empty(nbytes, device=dev, dtype=torch.uint8)
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        _lib.check(L.kb200_attn_fp8_fwd(qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), o.data_ptr(), B, S,
+                                        num_heads, D, float(softmax_scale), int(two_term),
+                                        ws.data_ptr(), nbytes, stream),
+                   'attention_fp8')
+    return o
+
+
+class AttentionModule(nn.Module):
+    """Drop-in for ``AttentionModule`` / ``SageAttention3Module`` (``kairos_dit.py:362-420``)."""
+
+    def __init__(self, num_heads, two_term: bool = True):
+        super().__init__()
+        self.num_heads = num_heads
+        self.two_term = two_term
+
+    def forward(self, q, k, v, attn_mask=None, window_size=(-1, -1)):
+        if attn_mask is not None:
+            raise NotImplementedError('FP8 attention path does not support arbitrary attn_mask')
+        if tuple(window_size) != (-1, -1):
+            raise NotImplementedError('FP8 attention path does not implement windowed attention')
+        return attention_fp8(q, k, v, self.num_heads, two_term=self.two_term)
+
+
+FP8AttentionModule = AttentionModule

@@ -1,6 +1,7 @@
 // common.cuh -- small device helpers shared by the kb200 kernels (sm_100a).
 #pragma once
 #include <cuda_runtime.h>
+#include <cuda_fp16.h>
 #include <cuda_bf16.h>
 #include <cuda_fp8.h>
 #include <stdint.h>
