@@ -1,0 +1,246 @@
+#!/usr/bin/env python
+"""Benchmark of the hybrid block at T = 32760 tokens.
+
+One step = the GDN mixer chain followed by the FP8-attention mixer chain of
+``kairos_sensenova_b200.hybrid.HybridBlock`` over the whole sequence, Ulysses
+sequence-parallel over N GPUs (one process per GPU, NCCL).  Metric: hybrid
+block Mtokens/s = T / step time.  Synthetic seeded N(0,1) hidden states
+[32760, 3072] bf16, random-init N(0,0.02) weights (no checkpoints exist here).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+For N > 1 launch with torch.distributed.run (127.0.0.1 rendezvous).
+``--impl reference`` times the reference path's CPU restatement (the oracle
+port of the reference's torch code) on this host's cores, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+import torch.distributed as dist
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+T_FULL, HIDDEN, HEADS, HEAD_DIM = 32760, 3072, 24, 128
+METRIC = 'hybrid-block Mtokens/s @T=32760 bf16'
+
+
+def _peaks():
+    p = ROOT / 'MEASURED_PEAKS.json'
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d['bf16_tflops'], d['hbm_gbs'], 'measured'
+    return 1590.0, 6650.0, 'fallback'
+
+
+def _cpu_sample_seconds(reps=1):
+    """Time one bounded CPU sample: the hybrid chain for 1 of the 24 heads over
+    the full sequence (the per-head share of every projection included), with
+    the oracle restatement of the reference's torch code.  Returns seconds."""
+    from oracle.hybrid import attn_chain, gdn_chain
+    torch.set_num_threads(os.cpu_count())
+    g = torch.Generator().manual_seed(0)
+    H, D = HEADS, HEAD_DIM
+    w = {n: torch.randn(HEADS * HEAD_DIM, HIDDEN, generator=g) * 0.02 for n in ('Wq', 'Wk', 'Wv', 'Wg', 'Aq', 'Ak', 'Av')}
+    w['Wo'] = torch.randn(HIDDEN, HEADS * HEAD_DIM, generator=g) * 0.02
+    w['Ao'] = torch.randn(HIDDEN, HEADS * HEAD_DIM, generator=g) * 0.02
+    w['Wa'] = torch.randn(HEADS, HIDDEN, generator=g) * 0.02
+    w['Wb'] = torch.randn(HEADS, HIDDEN, generator=g) * 0.02
+    for n in ('cq', 'ck', 'cv'):
+        w[n] = torch.rand(HEADS * HEAD_DIM, 4, generator=g) - 0.5
+    w['A_log'] = torch.log(torch.rand(HEADS, generator=g) * 16)
+    w['dt_bias'] = torch.randn(HEADS, generator=g) * 0.1 - 3
+    w['o_norm_w'] = torch.ones(HEAD_DIM)
+    x = torch.randn(T_FULL, HIDDEN, generator=g).bfloat16().float()
+    times = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        with torch.no_grad():
+            y = gdn_chain(w, x, H, D, heads=[0])
+            attn_chain(w, y, H, D, heads=[0])
+        times.append(time.perf_counter() - t0)
+    return times
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    def __init__(self, gpu_index):
+        self.proc = None
+        self.path = Path('/tmp') / f'kb200_clocks_{os.getpid()}.csv'
+        try:
+            self.proc = subprocess.Popen(
+                ['nvidia-smi', f'--id={gpu_index}',
+                 '--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.active,'
+                 'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
+                 'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap',
+                 '--format=csv,noheader,nounits', '-lms', '200'],
+                stdout=open(self.path, 'w'), stderr=subprocess.DEVNULL)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = [r.split(',') for r in self.path.read_text().strip().splitlines() if r.strip()]
+        sm, mx, reasons = [], 0.0, set()
+        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
+        for r in rows:
+            try:
+                sm.append(float(r[0]))
+                mx = max(mx, float(r[1]))
+                for n, v in zip(names, r[3:7]):
+                    if v.strip().lower() == 'active':
+                        reasons.add(n)
+            except (ValueError, IndexError):
+                continue
+        return {'sm_mhz': statistics.median(sm) if sm else None, 'sm_max_mhz': mx or None,
+                'reasons': sorted(reasons), 'samples': len(sm)}
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    times = _cpu_sample_seconds(args.warmup + args.steps)[args.warmup:]
+    step_s = statistics.mean(times) * HEADS        # the sample is 1/24 of a step's work
+    v = T_FULL / step_s / 1e6
+    cores = os.cpu_count()
+    line = {
+        'impl': 'reference', 'metric': METRIC, 'value': v, 'unit': 'Mtokens/s',
+        'n_gpus': args.gpus, 'steps': args.steps, 'warmup': args.warmup,
+        'ms_per_step': step_s * 1e3, 'higher_is_better': True, 'scaling': 'weak',
+        'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
+        'config': {'workload': 'config3 hybrid block (GDN chain + attention chain), T=32760, '
+                               'hidden 3072, 24x128 heads', 'global_batch': 1, 'seq_len': T_FULL,
+                   'parallelism': 'cpu'},
+        'cpu_baseline': {'value': v, 'unit': 'Mtokens/s', 'cores': cores, 'kind': 'port',
+                         'sample': 'hybrid chain for 1 of 24 heads over the full T=32760 '
+                                   '(per-head share of all projections), x24'},
+        'e2e': {'value': v, 'unit': 'Mtokens/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument('--gpus', type=int, default=1)
+    ap.add_argument('--steps', type=int, default=10)
+    ap.add_argument('--warmup', type=int, default=3)
+    ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
+    ap.add_argument('--single-term', action='store_true', help='single-term e4m3 attention')
+    ap.add_argument('--no-cpu-baseline', action='store_true')
+    args = ap.parse_args()
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    if args.impl == 'reference':
+        run_reference(args, rank)
+        return
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group('nccl', device_id=torch.device('cuda', local))
+    from kairos_sensenova_b200.hybrid import HybridBlock
+    assert T_FULL % world == 0 and HEADS % world == 0
+    Tl = T_FULL // world
+    blk = HybridBlock(HIDDEN, HEADS, HEAD_DIM, world=world, rank=rank, group=None,
+                      two_term=not args.single_term)
+    gen = torch.Generator(device='cuda')
+    gen.manual_seed(2)
+    x_full = torch.randn(T_FULL, HIDDEN, generator=gen, device='cuda').to(torch.bfloat16)
+    x = x_full[rank * Tl:(rank + 1) * Tl].contiguous()
+    del x_full
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device='cuda')   # > 126 MB L2
+
+    def sync_all():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            blk.forward(x)
+        sync_all()
+        sampler = ClockSampler(local) if rank == 0 else None
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+               torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(args.steps)]
+        sync_all()
+        for s0, s1, a0, a1 in ev:
+            flush.zero_()                       # L2 flush between timed steps (outside the events)
+            s0.record()
+            blk.forward(x, events=(a0, a1))
+            s1.record()
+        sync_all()
+        step_ms = statistics.mean(s0.elapsed_time(s1) for s0, s1, _, _ in ev)
+        attn_ms = statistics.mean(a0.elapsed_time(a1) for _, _, a0, a1 in ev)
+        # end to end through the public API with host buffers
+        xh = x.cpu().pin_memory()
+        yh = torch.empty(Tl, HIDDEN, dtype=torch.bfloat16).pin_memory()
+        sync_all()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            xd = xh.to('cuda', non_blocking=True)
+            yh.copy_(blk.forward(xd), non_blocking=True)
+        e1.record()
+        sync_all()
+        e2e_ms = e0.elapsed_time(e1) / args.steps
+        clocks = sampler.stop() if sampler else None
+
+    t = torch.tensor([step_ms, attn_ms, e2e_ms], device='cuda')
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    step_ms, attn_ms, e2e_ms = t.tolist()
+    if rank == 0:
+        bf16_tf, hbm, kind = _peaks()
+        fp8_peak = 2 * bf16_tf
+        flops = 4.0 * T_FULL * T_FULL * HEAD_DIM * (HEADS // world)
+        achieved = flops / (attn_ms * 1e-3) / 1e12
+        line = {
+            'metric': METRIC, 'value': T_FULL / (step_ms * 1e-3) / 1e6, 'unit': 'Mtokens/s',
+            'n_gpus': world, 'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': step_ms,
+            'higher_is_better': True, 'scaling': 'strong', 'vs_baseline': None, 'dtype': 'bf16/e4m3',
+            'data': 'synthetic',
+            'config': {'workload': 'config3 hybrid block: GDN chain + FP8-attention chain, T=32760, '
+                                   'hidden 3072, 24x128 heads, Ulysses over ranks',
+                       'global_batch': 1, 'seq_len': T_FULL, 'parallelism': f'ulysses{world}',
+                       'attention_terms': 1 if args.single_term else 2,
+                       'l2': 'flushed (256 MB write) between timed steps'},
+            'e2e': {'value': T_FULL / (e2e_ms * 1e-3) / 1e6, 'unit': 'Mtokens/s',
+                    'h2d_bytes_per_step': Tl * HIDDEN * 2, 'd2h_bytes_per_step': Tl * HIDDEN * 2},
+            'gpu_launches': blk.LAUNCHES_PER_STEP * args.steps,
+            'roofline': {'kernel': 'attention (fp8)', 'bound': 'tensor', 'achieved': achieved,
+                         'peak': fp8_peak, 'unit': 'TFLOP/s', 'frac': achieved / fp8_peak,
+                         'traffic': None, 'attn_ms': attn_ms,
+                         'peak_source': f'2x {kind} bf16 dense ({bf16_tf} TFLOP/s): FP8 dense rate'},
+            'clocks': clocks,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            ts = _cpu_sample_seconds(2)
+            s = min(ts) * HEADS
+            line['cpu_baseline'] = {'value': T_FULL / s / 1e6, 'unit': 'Mtokens/s', 'cores': os.cpu_count(),
+                                    'kind': 'port',
+                                    'sample': 'oracle hybrid chain, 1 of 24 heads over the full T=32760 '
+                                              '(per-head share of all projections), scaled x24'}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == '__main__':
+    main()

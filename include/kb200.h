@@ -88,6 +88,55 @@ size_t kb200_attn_fp8_workspace_size(int64_t B, int64_t S, int64_t H, int64_t D,
 int kb200_attn_fp8_fwd(const void* q, const void* k, const void* v, void* o, int64_t B, int64_t S,
                        int64_t H, int64_t D, float softmax_scale, int two_term, void* workspace,
                        size_t workspace_bytes, void* stream);
+/* The two halves of kb200_attn_fp8_fwd, for callers that time or overlap them
+ * separately: _quantize fills the workspace (amax, e4m3 q/k/v^T), _attend reads
+ * it and writes o.  Same arguments; _attend must follow a _quantize of the
+ * same inputs into the same workspace on the same stream. */
+int kb200_attn_fp8_quantize(const void* q, const void* k, const void* v, void* o, int64_t B,
+                            int64_t S, int64_t H, int64_t D, float softmax_scale, int two_term,
+                            void* workspace, size_t workspace_bytes, void* stream);
+int kb200_attn_fp8_attend(const void* q, const void* k, const void* v, void* o, int64_t B,
+                          int64_t S, int64_t H, int64_t D, float softmax_scale, int two_term,
+                          void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------
+ * GatedDeltaNet prologue in one launch: short causal depthwise convolutions
+ * + SiLU for q, k, v and the beta / g gates.
+ * Replaces (kairos/third_party/fla/layers/gated_deltanet.py):
+ *   :238-255  ShortConvolution q/k/v (causal_conv1d_fwd, fla/modules/convolution.py:410)
+ *   :267-271  beta = sigmoid(b_proj(x)) (x2 if allow_neg_eigval);
+ *             g = -exp(A_log) * softplus(a_proj(x) + dt_bias), fp32
+ * Inputs are the projection outputs (rows of B*T tokens, row strides ld* in
+ * elements, so q/k/v may be column slices of one fused projection).
+ * --------------------------------------------------------------------- */
+typedef struct KB200GdnPrologueArgs {
+  const void* xq; const void* xk; const void* xv;   /* bf16 [B*T, C] rows, stride ld*       */
+  int64_t ldq, ldk, ldv;
+  const float* wq; const float* wk; const float* wv; /* conv weights [C, W] fp32            */
+  const float* bq; const float* bk; const float* bv; /* conv bias [C] or NULL               */
+  void* q; void* k; void* v;                         /* out bf16 [B*T, C] contiguous         */
+  const void* a; const void* b;                      /* bf16 [B*T, H] rows, strides lda/ldb  */
+  int64_t lda, ldb;
+  const float* A_log; const float* dt_bias;          /* [H] fp32                             */
+  float* g;                                          /* out [B*T, H] fp32                    */
+  void* beta;                                        /* out [B*T, H] bf16                    */
+  int64_t B, T, H, Cqk, Cv;
+  int W;                                             /* conv width, 1..4                     */
+  int allow_neg_eigval;
+} KB200GdnPrologueArgs;
+int kb200_gdn_prologue(const KB200GdnPrologueArgs* a, void* stream);
+
+/* ---------------------------------------------------------------------
+ * Gated RMSNorm epilogue: y = x * rsqrt(mean(x^2) + eps) * weight * silu(gate)
+ * per row of D channels.  Replaces FusedRMSNormGated.forward with
+ * activation 'swish' (kairos/third_party/fla/modules/fused_norm_gate.py:1024-1085,
+ * kernel :60-110) as called at gated_deltanet.py:309-311.
+ * x, y: [rows, D] bf16 with rows = tokens * heads; gate: bf16, row (token) stride
+ * ld_gate elements, head h at column h*D; weight: [D] fp32.
+ * --------------------------------------------------------------------- */
+int kb200_rmsnorm_gated(const void* x, const void* gate, const float* weight, void* y,
+                        int64_t rows, int64_t heads, int64_t D, int64_t ld_gate, float eps,
+                        void* stream);
 
 #ifdef __cplusplus
 }

@@ -32,6 +32,27 @@ class GdnArgs(ctypes.Structure):
     ]
 
 
+class GdnPrologueArgs(ctypes.Structure):
+    """Mirror of ``KB200GdnPrologueArgs`` (include/kb200.h)."""
+    _fields_ = [
+        ('xq', ctypes.c_void_p), ('xk', ctypes.c_void_p), ('xv', ctypes.c_void_p),
+        ('ldq', ctypes.c_int64), ('ldk', ctypes.c_int64), ('ldv', ctypes.c_int64),
+        ('wq', ctypes.c_void_p), ('wk', ctypes.c_void_p), ('wv', ctypes.c_void_p),
+        ('bq', ctypes.c_void_p), ('bk', ctypes.c_void_p), ('bv', ctypes.c_void_p),
+        ('q', ctypes.c_void_p), ('k', ctypes.c_void_p), ('v', ctypes.c_void_p),
+        ('a', ctypes.c_void_p), ('b', ctypes.c_void_p),
+        ('lda', ctypes.c_int64), ('ldb', ctypes.c_int64),
+        ('A_log', ctypes.c_void_p), ('dt_bias', ctypes.c_void_p),
+        ('g', ctypes.c_void_p), ('beta', ctypes.c_void_p),
+        ('B', ctypes.c_int64), ('T', ctypes.c_int64), ('H', ctypes.c_int64),
+        ('Cqk', ctypes.c_int64), ('Cv', ctypes.c_int64),
+        ('W', ctypes.c_int), ('allow_neg_eigval', ctypes.c_int),
+    ]
+
+
+_ATTN_SIG = (ctypes.c_int, [ctypes.c_void_p] * 4 + [ctypes.c_int64] * 4 +
+             [ctypes.c_float, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p])
+
 # name -> (restype, argtypes); every symbol include/kb200.h declares
 SIGNATURES = {
     'kb200_abi_version': (ctypes.c_int, []),
@@ -40,9 +61,12 @@ SIGNATURES = {
     'kb200_gdn_chunk_fwd': (ctypes.c_int, [ctypes.POINTER(GdnArgs), ctypes.c_void_p,
                                            ctypes.c_size_t, ctypes.c_void_p]),
     'kb200_attn_fp8_workspace_size': (ctypes.c_size_t, [ctypes.c_int64] * 4 + [ctypes.c_int]),
-    'kb200_attn_fp8_fwd': (ctypes.c_int, [ctypes.c_void_p] * 4 + [ctypes.c_int64] * 4 +
-                           [ctypes.c_float, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t,
-                            ctypes.c_void_p]),
+    'kb200_attn_fp8_fwd': _ATTN_SIG,
+    'kb200_attn_fp8_quantize': _ATTN_SIG,
+    'kb200_attn_fp8_attend': _ATTN_SIG,
+    'kb200_gdn_prologue': (ctypes.c_int, [ctypes.POINTER(GdnPrologueArgs), ctypes.c_void_p]),
+    'kb200_rmsnorm_gated': (ctypes.c_int, [ctypes.c_void_p] * 4 + [ctypes.c_int64] * 4 +
+                            [ctypes.c_float, ctypes.c_void_p]),
 }
 
 

@@ -22,8 +22,12 @@ from . import _lib
 
 
 def attention_fp8(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, num_heads: int,
-                  softmax_scale: float | None = None, two_term: bool = True) -> torch.Tensor:
-    """q, k, v: [B, S, H*D] (bf16; other float dtypes are converted) -> [B, S, H*D] bf16."""
+                  softmax_scale: float | None = None, two_term: bool = True,
+                  events=None) -> torch.Tensor:
+    """q, k, v: [B, S, H*D] (bf16; other float dtypes are converted) -> [B, S, H*D] bf16.
+
+    ``events``: optional (start, end) CUDA events recorded on the launch stream
+    around the attention kernel alone (after quantisation)."""
     if q.device.type != 'cuda':
         raise RuntimeError('attention_fp8: inputs must be CUDA tensors (no CPU path)')
     if q.dim() != 3 or k.shape != q.shape or v.shape != q.shape:
@@ -45,10 +49,15 @@ def attention_fp8(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, num_heads: 
             raise ValueError(f'attention_fp8: unsupported shape B={B} S={S} H={num_heads} D={D} (D must be 128)')
         ws = torch.empty(nbytes, device=dev, dtype=torch.uint8)
         stream = torch.cuda.current_stream(dev).cuda_stream
-        _lib.check(L.kb200_attn_fp8_fwd(qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), o.data_ptr(), B, S,
-                                        num_heads, D, float(softmax_scale), int(two_term),
-                                        ws.data_ptr(), nbytes, stream),
-                   'attention_fp8')
+        args = (qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), o.data_ptr(), B, S, num_heads, D,
+                float(softmax_scale), int(two_term), ws.data_ptr(), nbytes, stream)
+        if events is None:
+            _lib.check(L.kb200_attn_fp8_fwd(*args), 'attention_fp8')
+        else:
+            _lib.check(L.kb200_attn_fp8_quantize(*args), 'attention_fp8 quantize')
+            events[0].record()
+            _lib.check(L.kb200_attn_fp8_attend(*args), 'attention_fp8 attend')
+            events[1].record()
     return o
 
 

@@ -377,20 +377,19 @@ extern "C" size_t kb200_attn_fp8_workspace_size(int64_t B, int64_t S, int64_t H,
   return attn_ws(B, S, H, two_term).total;
 }
 
-extern "C" int kb200_attn_fp8_fwd(const void* q, const void* k, const void* v, void* o, int64_t B,
-                                  int64_t S, int64_t H, int64_t D, float softmax_scale,
-                                  int two_term, void* workspace, size_t workspace_bytes,
-                                  void* stream) {
+namespace {
+int attn_setup(attn::Params& p, AttnWs& w, const void* q, const void* k, const void* v, void* o,
+               int64_t B, int64_t S, int64_t H, int64_t D, float softmax_scale, int two_term,
+               void* workspace, size_t workspace_bytes) {
   if (int e = attn_validate(q, k, v, o, B, S, H, D)) return e;
-  const AttnWs w = attn_ws(B, S, H, two_term);
+  w = attn_ws(B, S, H, two_term);
   if (!workspace || workspace_bytes < w.total)
     return set_error(KB200_ERR_WORKSPACE, "attn_fp8: workspace needs %zu bytes, got %zu", w.total,
                      workspace_bytes);
   if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
     return set_error(KB200_ERR_ALIGN, "attn_fp8: workspace must be 256-byte aligned");
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   char* ws = static_cast<char*>(workspace);
-  attn::Params p{};
+  p = attn::Params{};
   p.q = (const __nv_bfloat16*)q;
   p.k = (const __nv_bfloat16*)k;
   p.v = (const __nv_bfloat16*)v;
@@ -408,16 +407,52 @@ extern "C" int kb200_attn_fp8_fwd(const void* q, const void* k, const void* v, v
   p.softmax_scale = softmax_scale;
   p.vperm = 1;
   p.two_term = two_term ? 1 : 0;
-  if (cudaMemsetAsync(p.amax, 0, (size_t)3 * B * H * 4, st) != cudaSuccess)
+  return KB200_OK;
+}
+
+int attn_quantize(const attn::Params& p, const AttnWs& w, cudaStream_t st) {
+  if (cudaMemsetAsync(p.amax, 0, (size_t)3 * p.B * p.H * 4, st) != cudaSuccess)
     return check_launch("attn_fp8 amax memset");
-  attn::attn_amax_kernel<AD><<<dim3((unsigned)((S + 31) / 32), (unsigned)B), 256, 3 * H * 4, st>>>(p);
+  attn::attn_amax_kernel<AD><<<dim3((unsigned)((p.S + 31) / 32), (unsigned)p.B), 256, 3 * p.H * 4, st>>>(p);
   if (int e = check_launch("attn_amax_kernel")) return e;
-  attn::attn_quant_kernel<AD><<<dim3(w.S_pad / 64, (unsigned)(B * H)), 256, 0, st>>>(p);
-  if (int e = check_launch("attn_quant_kernel")) return e;
+  attn::attn_quant_kernel<AD><<<dim3(w.S_pad / 64, (unsigned)(p.B * p.H)), 256, 0, st>>>(p);
+  return check_launch("attn_quant_kernel");
+}
+
+int attn_attend(const attn::Params& p, const AttnWs& w, cudaStream_t st) {
   const size_t smem = sizeof(attn::MmaSmem<AD, ABM, ABN, ASTAGES>);
-  auto kern = two_term ? attn::attn_fp8_mma_kernel<AD, ABM, ABN, ASTAGES, 2>
-                       : attn::attn_fp8_mma_kernel<AD, ABM, ABN, ASTAGES, 1>;
+  auto kern = p.two_term ? attn::attn_fp8_mma_kernel<AD, ABM, ABN, ASTAGES, 2>
+                         : attn::attn_fp8_mma_kernel<AD, ABM, ABN, ASTAGES, 1>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  kern<<<dim3(w.S_pad / ABM, (unsigned)(B * H)), 256, smem, st>>>(p);
+  kern<<<dim3(w.S_pad / ABM, (unsigned)(p.B * p.H)), 256, smem, st>>>(p);
   return check_launch("attn_fp8_mma_kernel");
+}
+}  // namespace
+
+#define KB_ATTN_ARGS                                                                         \
+  const void *q, const void *k, const void *v, void *o, int64_t B, int64_t S, int64_t H,    \
+      int64_t D, float softmax_scale, int two_term, void *workspace, size_t workspace_bytes, \
+      void *stream
+#define KB_ATTN_SETUP                                                                          \
+  attn::Params p;                                                                              \
+  AttnWs w;                                                                                    \
+  if (int e = attn_setup(p, w, q, k, v, o, B, S, H, D, softmax_scale, two_term, workspace,     \
+                         workspace_bytes))                                                     \
+    return e;                                                                                  \
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+extern "C" int kb200_attn_fp8_fwd(KB_ATTN_ARGS) {
+  KB_ATTN_SETUP
+  if (int e = attn_quantize(p, w, st)) return e;
+  return attn_attend(p, w, st);
+}
+
+extern "C" int kb200_attn_fp8_quantize(KB_ATTN_ARGS) {
+  KB_ATTN_SETUP
+  return attn_quantize(p, w, st);
+}
+
+extern "C" int kb200_attn_fp8_attend(KB_ATTN_ARGS) {
+  KB_ATTN_SETUP
+  return attn_attend(p, w, st);
 }

@@ -1,0 +1,220 @@
+// layer_fusions.cu -- the GatedDeltaNet prologue and output-norm epilogue
+// as single memory-bound passes (sm_100a).
+//
+// Prologue (kairos/third_party/fla/layers/gated_deltanet.py:238-271):
+//   q, k, v = SiLU(causal depthwise conv_W(x) + bias)       (fla/modules/convolution.py:53-140)
+//   beta    = sigmoid(b)            (x2 when allow_neg_eigval)
+//   g       = -exp(A_log) * softplus(a + dt_bias)           in fp32
+// One launch covers the three convolutions and the gates (grid.z selects).
+//
+// Epilogue (gated_deltanet.py:309-311, FusedRMSNormGated,
+// fla/modules/fused_norm_gate.py:60-110 with activation 'swish'):
+//   y = o * rsqrt(mean(o^2) + eps) * w * gate * sigmoid(gate)   per (token, head) row
+#include "common.cuh"
+#include "kb200_internal.h"
+
+namespace kb {
+namespace fuse {
+
+struct ConvSet {
+  const __nv_bfloat16* x;
+  const float* w;     // [C, W]
+  const float* bias;  // [C] or null
+  __nv_bfloat16* y;
+  int C;
+  int64_t ldx, ldy;   // row strides in elements
+};
+
+struct PrologueParams {
+  ConvSet set[3];
+  const __nv_bfloat16* a;
+  const __nv_bfloat16* b;
+  int64_t lda, ldb;
+  const float* A_log;
+  const float* dt_bias;
+  float* g;
+  __nv_bfloat16* beta;
+  int B, T, H, W;
+  int allow_neg_eigval;
+};
+
+// Grid (ceil(T / 32), ceil(maxC / 256), B * 4): z = 4*b + {0,1,2: conv q,k,v; 3: gates}.
+// Conv: each thread owns 8 consecutive channels of one token (16-byte vectors);
+// the W-1 previous tokens come from L1/L2 (each input row is read W times).
+__global__ void __launch_bounds__(256) gdn_prologue_kernel(PrologueParams p) {
+  const int which = blockIdx.z & 3, bb = blockIdx.z >> 2;
+  const int tok0 = blockIdx.x * 32;
+  if (which < 3) {
+    const ConvSet cs = p.set[which];
+    const int c8 = (blockIdx.y * 32 + (threadIdx.x & 31)) * 8;
+    if (c8 >= cs.C) return;
+    float w[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) w[j][i] = (i < p.W) ? cs.w[(c8 + j) * p.W + i] : 0.f;
+    float bias[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) bias[j] = cs.bias ? cs.bias[c8 + j] : 0.f;
+    for (int tt = threadIdx.x >> 5; tt < 32; tt += 8) {
+      const int t = tok0 + tt;
+      if (t >= p.T) break;
+      float acc[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = bias[j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        if (i >= p.W) break;
+        const int ts = t - (p.W - 1) + i;
+        if (ts < 0) continue;
+        uint4 raw = *reinterpret_cast<const uint4*>(cs.x + ((size_t)bb * p.T + ts) * cs.ldx + c8);
+        const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] += __bfloat162float(e[j]) * w[j][i];
+      }
+      uint4 outv;
+      uint32_t* ov = reinterpret_cast<uint32_t*>(&outv);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float y0 = acc[2 * j], y1 = acc[2 * j + 1];
+        ov[j] = pack_bf16(y0 / (1.f + __expf(-y0)), y1 / (1.f + __expf(-y1)));
+      }
+      *reinterpret_cast<uint4*>(cs.y + ((size_t)bb * p.T + t) * cs.ldy + c8) = outv;
+    }
+  } else {
+    if (blockIdx.y != 0) return;
+    for (int idx = threadIdx.x; idx < 32 * p.H; idx += blockDim.x) {
+      const int t = tok0 + idx / p.H, h = idx % p.H;
+      if (t >= p.T) break;
+      const size_t row = (size_t)bb * p.T + t;
+      const float bv = __bfloat162float(p.b[row * p.ldb + h]);
+      float beta = 1.f / (1.f + expf(-bv));
+      beta = __bfloat162float(__float2bfloat16_rn(beta));   // sigmoid output in activation dtype
+      if (p.allow_neg_eigval) beta *= 2.f;
+      p.beta[row * p.H + h] = __float2bfloat16_rn(beta);
+      const float av = __bfloat162float(p.a[row * p.lda + h]) + p.dt_bias[h];
+      const float sp = av > 20.f ? av : log1pf(expf(av));   // F.softplus(beta=1, threshold=20)
+      p.g[row * p.H + h] = -expf(p.A_log[h]) * sp;
+    }
+  }
+}
+
+// One warp per (token, head) row of D channels (D = 32 * EPL).
+template <int EPL>
+__global__ void __launch_bounds__(256) rmsnorm_gated_kernel(const __nv_bfloat16* __restrict__ x,
+                                                            const __nv_bfloat16* __restrict__ gate,
+                                                            const float* __restrict__ w,
+                                                            __nv_bfloat16* __restrict__ y,
+                                                            int64_t rows, int heads, int64_t ldg,
+                                                            float eps) {
+  constexpr int D = 32 * EPL;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int64_t tok = row / heads, h = row % heads;
+  const __nv_bfloat16* xr = x + row * D + lane * EPL;
+  const __nv_bfloat16* gr = gate + tok * ldg + h * D + lane * EPL;
+  float xv[EPL], gv[EPL];
+#pragma unroll
+  for (int e = 0; e < EPL; e += 4) {
+    uint2 rx = *reinterpret_cast<const uint2*>(xr + e);
+    uint2 rg = *reinterpret_cast<const uint2*>(gr + e);
+    const __nv_bfloat16* ex = reinterpret_cast<const __nv_bfloat16*>(&rx);
+    const __nv_bfloat16* eg = reinterpret_cast<const __nv_bfloat16*>(&rg);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) { xv[e + j] = __bfloat162float(ex[j]); gv[e + j] = __bfloat162float(eg[j]); }
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) ss += xv[e] * xv[e];
+  ss = warp_sum(ss);
+  const float rstd = 1.f / sqrtf(ss / D + eps);
+#pragma unroll
+  for (int e = 0; e < EPL; e += 4) {
+    uint2 out;
+    uint32_t* o32 = reinterpret_cast<uint32_t*>(&out);
+#pragma unroll
+    for (int j = 0; j < 4; j += 2) {
+      float r[2];
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int ee = e + j + q;
+        const float gg = gv[ee];
+        r[q] = xv[ee] * rstd * w[lane * EPL + ee] * gg / (1.f + __expf(-gg));
+      }
+      o32[j / 2] = pack_bf16(r[0], r[1]);
+    }
+    *reinterpret_cast<uint2*>(y + row * D + lane * EPL + e) = out;
+  }
+}
+
+}  // namespace fuse
+}  // namespace kb
+
+// ===========================================================================
+// Host side: C ABI
+// ===========================================================================
+using namespace kb;
+
+extern "C" int kb200_gdn_prologue(const KB200GdnPrologueArgs* a, void* stream) {
+  if (!a) return set_error(KB200_ERR_INVALID, "gdn_prologue: null args");
+  if (a->B <= 0 || a->T <= 0 || a->H <= 0 || a->W < 1 || a->W > 4)
+    return set_error(KB200_ERR_INVALID, "gdn_prologue: bad shape (B,T,H > 0, 1 <= W <= 4)");
+  fuse::PrologueParams p{};
+  const void* xs[3] = {a->xq, a->xk, a->xv};
+  const float* ws[3] = {a->wq, a->wk, a->wv};
+  const float* bs[3] = {a->bq, a->bk, a->bv};
+  void* ys[3] = {a->q, a->k, a->v};
+  const int64_t cs[3] = {a->Cqk, a->Cqk, a->Cv};
+  const int64_t lx[3] = {a->ldq, a->ldk, a->ldv};
+  int maxc = 0;
+  for (int i = 0; i < 3; ++i) {
+    if (!xs[i] || !ws[i] || !ys[i]) return set_error(KB200_ERR_INVALID, "gdn_prologue: null tensor");
+    if (cs[i] <= 0 || cs[i] % 8 || lx[i] % 8 || !aligned16(xs[i]) || !aligned16(ys[i]))
+      return set_error(KB200_ERR_ALIGN, "gdn_prologue: channels/strides must be multiples of 8, rows 16-byte aligned");
+    p.set[i] = fuse::ConvSet{(const __nv_bfloat16*)xs[i], ws[i], bs[i], (__nv_bfloat16*)ys[i], (int)cs[i],
+                             lx[i], cs[i]};
+    maxc = maxc > (int)cs[i] ? maxc : (int)cs[i];
+  }
+  if (!a->a || !a->b || !a->A_log || !a->dt_bias || !a->g || !a->beta)
+    return set_error(KB200_ERR_INVALID, "gdn_prologue: null gate tensor");
+  p.a = (const __nv_bfloat16*)a->a;
+  p.b = (const __nv_bfloat16*)a->b;
+  p.lda = a->lda;
+  p.ldb = a->ldb;
+  p.A_log = a->A_log;
+  p.dt_bias = a->dt_bias;
+  p.g = a->g;
+  p.beta = (__nv_bfloat16*)a->beta;
+  p.B = (int)a->B;
+  p.T = (int)a->T;
+  p.H = (int)a->H;
+  p.W = a->W;
+  p.allow_neg_eigval = a->allow_neg_eigval;
+  dim3 grid((unsigned)((a->T + 31) / 32), (unsigned)((maxc / 8 + 31) / 32), (unsigned)(a->B * 4));
+  fuse::gdn_prologue_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  return check_launch("gdn_prologue_kernel");
+}
+
+extern "C" int kb200_rmsnorm_gated(const void* x, const void* gate, const float* weight, void* y,
+                                   int64_t rows, int64_t heads, int64_t D, int64_t ld_gate,
+                                   float eps, void* stream) {
+  if (!x || !gate || !weight || !y) return set_error(KB200_ERR_INVALID, "rmsnorm_gated: null pointer");
+  if (rows < 0 || heads <= 0 || rows % heads)
+    return set_error(KB200_ERR_INVALID, "rmsnorm_gated: rows must be a multiple of heads");
+  if (D != 128 && D != 256 && D != 512)
+    return set_error(KB200_ERR_INVALID, "rmsnorm_gated: D must be 128, 256 or 512");
+  if (ld_gate % 4 || !aligned16(x) || !aligned16(y) || (reinterpret_cast<uintptr_t>(gate) & 7))
+    return set_error(KB200_ERR_ALIGN, "rmsnorm_gated: misaligned tensor or gate stride");
+  if (rows == 0) return KB200_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const unsigned grid = (unsigned)((rows + 7) / 8);
+  const int hh = (int)heads;
+  const __nv_bfloat16* xb = (const __nv_bfloat16*)x;
+  const __nv_bfloat16* gb = (const __nv_bfloat16*)gate;
+  __nv_bfloat16* yb = (__nv_bfloat16*)y;
+  if (D == 128) fuse::rmsnorm_gated_kernel<4><<<grid, 256, 0, st>>>(xb, gb, weight, yb, rows, hh, ld_gate, eps);
+  else if (D == 256) fuse::rmsnorm_gated_kernel<8><<<grid, 256, 0, st>>>(xb, gb, weight, yb, rows, hh, ld_gate, eps);
+  else fuse::rmsnorm_gated_kernel<16><<<grid, 256, 0, st>>>(xb, gb, weight, yb, rows, hh, ld_gate, eps);
+  return check_launch("rmsnorm_gated_kernel");
+}

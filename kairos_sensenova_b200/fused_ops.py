@@ -1,0 +1,87 @@
+"""Python entry points of the prologue / epilogue fusion kernels.
+
+* :func:`gdn_prologue` -- ShortConvolution(q,k,v)+SiLU and the beta/g gates of
+  ``GatedDeltaNet.forward`` (``kairos/third_party/fla/layers/gated_deltanet.py:238-271``)
+  in one launch.
+* :func:`rms_norm_gated` -- ``FusedRMSNormGated`` (swish gate) forward
+  (``fla/modules/fused_norm_gate.py:1024-1085``).
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+
+def _stream(dev):
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _rows(x, C):
+    """Validate a [*, C] bf16 row view with unit column stride; return (tensor, row stride)."""
+    if x.dtype != torch.bfloat16:
+        x = x.to(torch.bfloat16)
+    x2 = x.reshape(-1, C) if x.is_contiguous() else x
+    if x2.dim() != 2 or x2.stride(-1) != 1:
+        x2 = x2.contiguous().reshape(-1, C)
+    return x2, x2.stride(0)
+
+
+def gdn_prologue(xq, xk, xv, a, b, wq, wk, wv, A_log, dt_bias, num_heads, B, T,
+                 bq=None, bk=None, bv=None, allow_neg_eigval=False):
+    """xq/xk/xv: bf16 [B*T, C] row views (may be column slices of one fused
+    projection), a/b: bf16 [B*T, H] row views, conv weights [C, W].
+    Returns q, k [B,T,H,Cqk/H], v [B,T,H,Cv/H] bf16, g fp32 [B,T,H], beta bf16 [B,T,H]."""
+    dev = xq.device
+    if dev.type != 'cuda':
+        raise RuntimeError('gdn_prologue: CUDA tensors required (no CPU path)')
+    Cqk, Cv = wq.shape[0], wv.shape[0]
+    W = wq.shape[-1]
+    H = num_heads
+    xq, ldq = _rows(xq, Cqk)
+    xk, ldk = _rows(xk, Cqk)
+    xv, ldv = _rows(xv, Cv)
+    a, lda = _rows(a, H)
+    b, ldb = _rows(b, H)
+    f32 = lambda t: None if t is None else t.to(device=dev, dtype=torch.float32).reshape(t.shape[0], -1).contiguous()  # noqa: E731
+    wq, wk, wv = f32(wq), f32(wk), f32(wv)
+    bq, bk, bv = (None if t is None else t.to(dev, torch.float32).contiguous() for t in (bq, bk, bv))
+    A = A_log.to(dev, torch.float32).contiguous()
+    dtb = dt_bias.to(dev, torch.float32).contiguous()
+    q = torch.empty(B, T, H, Cqk // H, device=dev, dtype=torch.bfloat16)
+    k = torch.empty_like(q)
+    v = torch.empty(B, T, H, Cv // H, device=dev, dtype=torch.bfloat16)
+    g = torch.empty(B, T, H, device=dev, dtype=torch.float32)
+    beta = torch.empty(B, T, H, device=dev, dtype=torch.bfloat16)
+    p = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+    args = _lib.GdnPrologueArgs(
+        xq=p(xq), xk=p(xk), xv=p(xv), ldq=ldq, ldk=ldk, ldv=ldv, wq=p(wq), wk=p(wk), wv=p(wv),
+        bq=p(bq), bk=p(bk), bv=p(bv), q=p(q), k=p(k), v=p(v), a=p(a), b=p(b), lda=lda, ldb=ldb,
+        A_log=p(A), dt_bias=p(dtb), g=p(g), beta=p(beta), B=B, T=T, H=H, Cqk=Cqk, Cv=Cv, W=W,
+        allow_neg_eigval=int(bool(allow_neg_eigval)))
+    with torch.cuda.device(dev):
+        _lib.check(_lib.lib().kb200_gdn_prologue(ctypes.byref(args), _stream(dev)), 'gdn_prologue')
+    return q, k, v, g, beta
+
+
+def rms_norm_gated(x: torch.Tensor, gate: torch.Tensor, weight: torch.Tensor, eps: float = 1e-5):
+    """x: [..., H, D] bf16; gate: same logical shape (token rows may be strided);
+    weight [D].  Returns bf16 like x."""
+    dev = x.device
+    if dev.type != 'cuda':
+        raise RuntimeError('rms_norm_gated: CUDA tensors required (no CPU path)')
+    D = x.shape[-1]
+    H = x.shape[-2] if x.dim() >= 2 else 1
+    xc = x.to(torch.bfloat16).contiguous()
+    g2 = gate.to(torch.bfloat16)
+    g2 = g2.reshape(-1, H * D) if g2.is_contiguous() else g2.contiguous().reshape(-1, H * D)
+    w = weight.to(dev, torch.float32).contiguous()
+    y = torch.empty_like(xc)
+    rows = xc.numel() // D
+    with torch.cuda.device(dev):
+        _lib.check(_lib.lib().kb200_rmsnorm_gated(xc.data_ptr(), g2.data_ptr(), w.data_ptr(), y.data_ptr(),
+                                                   rows, H, D, g2.stride(0), float(eps), _stream(dev)),
+                   'rms_norm_gated')
+    return y

@@ -1,0 +1,85 @@
+"""GPU parity of the prologue / epilogue fusion kernels and the GatedDeltaNet
+layer drop-in against the CPU oracle (oracle.layers)."""
+import pytest
+import torch
+
+from conftest import max_rel
+from oracle import layers as ol
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize('T', [1, 3, 70, 513])
+def test_prologue_matches_oracle(T):
+    from kairos_sensenova_b200.fused_ops import gdn_prologue
+    gen = torch.Generator().manual_seed(T)
+    B, H, K, V = 2, 3, 128, 256
+    xq = torch.randn(B * T, H * K, generator=gen).bfloat16()
+    xk = torch.randn(B * T, H * K, generator=gen).bfloat16()
+    xv = torch.randn(B * T, H * V, generator=gen).bfloat16()
+    a = torch.randn(B * T, H, generator=gen).bfloat16()
+    b = torch.randn(B * T, H, generator=gen).bfloat16()
+    wq, wk, wv = (torch.randn(c, 4, generator=gen) * 0.5 for c in (H * K, H * K, H * V))
+    A_log = torch.rand(H, generator=gen) * 2
+    dt_bias = torch.randn(H, generator=gen)
+    c = lambda t: t.cuda()  # noqa: E731
+    q, k, v, g, beta = gdn_prologue(c(xq), c(xk), c(xv), c(a), c(b), c(wq), c(wk), c(wv), c(A_log),
+                                    c(dt_bias), H, B, T)
+    ref = lambda x, w: ol.short_conv_silu(x.reshape(B, T, -1), w)  # noqa: E731
+    assert max_rel(q.reshape(B, T, -1), ref(xq, wq)) < 1e-2
+    assert max_rel(k.reshape(B, T, -1), ref(xk, wk)) < 1e-2
+    assert max_rel(v.reshape(B, T, -1), ref(xv, wv)) < 1e-2
+    gr, br = ol.gates(a, b, A_log, dt_bias)
+    assert max_rel(g.reshape(-1, H), gr) < 1e-5
+    assert max_rel(beta.reshape(-1, H), br) < 1e-2
+
+
+def test_prologue_strided_fused_projection():
+    """q/k/v/a/b given as column slices of one fused projection output."""
+    from kairos_sensenova_b200.fused_ops import gdn_prologue
+    gen = torch.Generator().manual_seed(1)
+    B, T, H, K = 1, 100, 2, 128
+    C = 3 * H * K + 2 * H + 4          # padded like the Ulysses-packed layout
+    proj = torch.randn(T, C, generator=gen).bfloat16().cuda()
+    w = torch.randn(H * K, 4, generator=gen).cuda()
+    A_log, dtb = torch.zeros(H).cuda(), torch.zeros(H).cuda()
+    s = lambda i: proj[:, i * H * K:(i + 1) * H * K]  # noqa: E731
+    ab = 3 * H * K
+    q, k, v, g, beta = gdn_prologue(s(0), s(1), s(2), proj[:, ab:ab + H], proj[:, ab + H:ab + 2 * H],
+                                    w, w, w, A_log, dtb, H, B, T)
+    q2, k2, v2, g2, b2 = gdn_prologue(s(0).contiguous(), s(1).contiguous(), s(2).contiguous(),
+                                      proj[:, ab:ab + H].contiguous(), proj[:, ab + H:ab + 2 * H].contiguous(),
+                                      w, w, w, A_log, dtb, H, B, T)
+    for x, y in ((q, q2), (k, k2), (v, v2), (g, g2), (beta, b2)):
+        assert torch.equal(x, y)
+
+
+@pytest.mark.parametrize('D', [128, 256])
+def test_rmsnorm_gated_matches_oracle(D):
+    from kairos_sensenova_b200.fused_ops import rms_norm_gated
+    gen = torch.Generator().manual_seed(D)
+    x = torch.randn(5, 7, 3, D, generator=gen).bfloat16()
+    gt = torch.randn(5, 7, 3, D, generator=gen).bfloat16()
+    w = torch.rand(D, generator=gen) + 0.5
+    y = rms_norm_gated(x.cuda(), gt.cuda(), w.cuda(), 1e-5)
+    assert y.dtype == torch.bfloat16
+    assert max_rel(y, ol.rmsnorm_gated(x, gt, w, 1e-5)) < 1e-2
+
+
+def test_gated_deltanet_layer_matches_oracle():
+    from kairos_sensenova_b200.layers import GatedDeltaNet
+    torch.manual_seed(0)
+    hidden, H, hd = 512, 4, 128
+    layer = GatedDeltaNet(hidden_size=hidden, expand_v=1, head_dim=hd, num_heads=H)
+    with torch.no_grad():
+        for n, p_ in layer.named_parameters():
+            if n.endswith('proj.weight'):
+                p_.normal_(0, 0.02)
+    sd = {k: v.detach().clone() for k, v in layer.state_dict().items()}
+    layer = layer.cuda().to(torch.bfloat16)
+    x = torch.randn(1, 300, hidden).bfloat16()
+    with torch.no_grad():
+        o, _, _ = layer(x.cuda())
+    ref = ol.gated_deltanet_forward({k: v.bfloat16().float() for k, v in sd.items()}, x.float(), H, hd, hd)
+    assert o.shape == (1, 300, hidden)
+    assert max_rel(o, ref) < 2e-2
