@@ -71,6 +71,22 @@ size_t kb200_gdn_workspace_size(const KB200GdnArgs* a);
 int kb200_gdn_chunk_fwd(const KB200GdnArgs* a, void* workspace, size_t workspace_bytes,
                         void* stream);
 
+/* Allocation-free variant of kb200_gdn_chunk_fwd (no counterpart in the
+ * reference).  For callers that cannot allocate device memory when they run
+ * the operator (a plugin host that owns all device memory, code in a host
+ * callback): the scratch comes from a 64 MiB array compiled into this
+ * library, which every GPU that loads the library keeps until process exit.
+ * Problems needing more scratch than kb200_gdn_noalloc_scratch_bytes()
+ * are rejected with KB200_ERR_WORKSPACE.  The first call on a device looks up
+ * the array's device address (cudaGetSymbolAddress) with that device
+ * current; make that first call before any stream capture.  All calls share
+ * the one array: calls that overlap on the GPU (different streams, or
+ * different threads on one device) race and must be serialised by the caller.
+ * Nothing in the array needs to start at zero, so stale contents from an
+ * earlier call do not matter.  Makes no cudaMalloc/cudaFree call. */
+size_t kb200_gdn_noalloc_scratch_bytes(void);
+int kb200_gdn_chunk_fwd_noalloc(const KB200GdnArgs* a, void* stream);
+
 /* ---------------------------------------------------------------------
  * Softmax attention with FP8-e4m3 Q/K/V, per-(batch, head) amax scaling
  * (scale = amax/448), fp32 softmax and accumulation, bf16 output.

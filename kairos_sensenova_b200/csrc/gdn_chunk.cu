@@ -741,3 +741,68 @@ extern "C" int kb200_gdn_chunk_fwd(const KB200GdnArgs* a, void* workspace, size_
 #undef KB_GDN_CASE
   return kb::set_error(KB200_ERR_INVALID, "gdn: unsupported dims");
 }
+
+// ===========================================================================
+// Allocation-free variant of kb200_gdn_chunk_fwd.
+//
+// Some callers cannot call cudaMalloc (or ask an allocator) at the point where
+// they run the operator -- for example code running inside a host callback or
+// a plugin host that owns all device memory and hands out only inputs and
+// outputs.  For them this entry point takes its scratch from a fixed,
+// file-scope device array instead of a caller-provided workspace.  The array
+// lives in every GPU that loads this library until the process exits.
+// ===========================================================================
+#include <mutex>
+
+namespace {
+constexpr size_t kGdnNoAllocScratchBytes = size_t(64) << 20;   // 64 MiB per device
+static __device__ __align__(256) unsigned char g_gdn_noalloc_scratch[kGdnNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of the scratch array on the current device (looked up once per device).
+int noalloc_scratch(void** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return set_error(KB200_ERR_LAUNCH, "gdn_noalloc: no usable current CUDA device");
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_gdn_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return set_error(KB200_ERR_LAUNCH, "gdn_noalloc: cudaGetSymbolAddress failed: %s",
+                       cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return KB200_OK;
+}
+}  // namespace
+
+extern "C" size_t kb200_gdn_noalloc_scratch_bytes(void) { return kGdnNoAllocScratchBytes; }
+
+extern "C" int kb200_gdn_chunk_fwd_noalloc(const KB200GdnArgs* a, void* stream) {
+  if (int e = validate(a)) return e;
+  const WsLayout L = ws_layout(a);
+  if (L.total > kGdnNoAllocScratchBytes)
+    return kb::set_error(KB200_ERR_WORKSPACE,
+                         "gdn_noalloc: problem needs %zu bytes of scratch, the built-in array "
+                         "holds %zu; use kb200_gdn_chunk_fwd with a caller workspace",
+                         L.total, kGdnNoAllocScratchBytes);
+  void* ws = nullptr;
+  if (int e = noalloc_scratch(&ws)) return e;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  char* w = static_cast<char*>(ws);
+#define KB_GDN_CASE(KK, VV) \
+  if (a->K == KK && a->V == VV) return launch<KK, VV>(a, L, w, st);
+  KB_GDN_CASE(128, 128)
+  KB_GDN_CASE(128, 256)
+  KB_GDN_CASE(128, 512)
+  KB_GDN_CASE(256, 128)
+  KB_GDN_CASE(256, 256)
+  KB_GDN_CASE(256, 512)
+#undef KB_GDN_CASE
+  return kb::set_error(KB200_ERR_INVALID, "gdn_noalloc: unsupported dims");
+}
