@@ -114,6 +114,11 @@ int kb200_attn_fp8_quantize(const void* q, const void* k, const void* v, void* o
 int kb200_attn_fp8_attend(const void* q, const void* k, const void* v, void* o, int64_t B,
                           int64_t S, int64_t H, int64_t D, float softmax_scale, int two_term,
                           void* workspace, size_t workspace_bytes, void* stream);
+/* Synchronises `stream` and reports KB200_ERR_TIMEOUT if a bounded device-side
+ * wait of the last attention launch on `workspace` gave up (the kernel then
+ * skipped its remaining work instead of hanging). */
+int kb200_attn_fp8_status(const void* workspace, int64_t B, int64_t S, int64_t H, int two_term,
+                          void* stream);
 
 /* ---------------------------------------------------------------------
  * GatedDeltaNet prologue in one launch: short causal depthwise convolutions

@@ -23,7 +23,7 @@ from . import _lib
 
 def attention_fp8(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, num_heads: int,
                   softmax_scale: float | None = None, two_term: bool = True,
-                  events=None) -> torch.Tensor:
+                  events=None, check: bool = False) -> torch.Tensor:
     """q, k, v: [B, S, H*D] (bf16; other float dtypes are converted) -> [B, S, H*D] bf16.
 
     ``events``: optional (start, end) CUDA events recorded on the launch stream
@@ -58,6 +58,9 @@ def attention_fp8(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, num_heads: 
             events[0].record()
             _lib.check(L.kb200_attn_fp8_attend(*args), 'attention_fp8 attend')
             events[1].record()
+        if check:   # synchronises; raises if a bounded device wait gave up
+            _lib.check(L.kb200_attn_fp8_status(ws.data_ptr(), B, S, num_heads, int(two_term), stream),
+                       'attention_fp8')
     return o
 
 

@@ -36,5 +36,8 @@ KB_DEVI float e4m3_to_float(uint8_t b) {
 
 KB_DEVI float scale_of(float amax) { return amax > 0.f ? amax / E4M3_MAX : 1.f; }
 
+// tcgen05 attention launcher (attn_fp8_tc.cu); V^T must be unpermuted (vperm = 0).
+int launch_attn_tc(const Params& p, int* err, cudaStream_t st);
+
 }  // namespace attn
 }  // namespace kb

@@ -18,6 +18,7 @@
 #include "common.cuh"
 #include "kb200_internal.h"
 #include "attn_common.cuh"
+#include <cstdlib>
 
 namespace kb {
 namespace attn {
@@ -338,7 +339,7 @@ namespace {
 using namespace kb;
 constexpr int AD = 128, ABM = 128, ABN = 64, ASTAGES = 3;
 
-struct AttnWs { size_t q8, k8, vt8, q8r, vt8r, amax, total; int S_pad; };
+struct AttnWs { size_t q8, k8, vt8, q8r, vt8r, amax, err, total; int S_pad; };
 
 AttnWs attn_ws(int64_t B, int64_t S, int64_t H, int two_term) {
   AttnWs w{};
@@ -351,7 +352,8 @@ AttnWs attn_ws(int64_t B, int64_t S, int64_t H, int two_term) {
   w.vt8 = take(n);
   w.q8r = take(two_term ? n : 0);
   w.vt8r = take(two_term ? n : 0);
-  w.amax = take((size_t)3 * B * H * 4);
+  w.amax = take((size_t)3 * B * H * 4 + 16);   // amax, then the device error word
+  w.err = w.amax + (size_t)3 * B * H * 4;
   w.total = off;
   return w;
 }
@@ -378,6 +380,17 @@ extern "C" size_t kb200_attn_fp8_workspace_size(int64_t B, int64_t S, int64_t H,
 }
 
 namespace {
+// KB200_ATTN_MMA_SYNC=1 selects the mma.sync kernel (kept only for A/B timing while the
+// tcgen05 kernel is brought up).
+bool use_tc() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("KB200_ATTN_MMA_SYNC");
+    v = (e && e[0] == '1') ? 0 : 1;
+  }
+  return v == 1;
+}
+
 int attn_setup(attn::Params& p, AttnWs& w, const void* q, const void* k, const void* v, void* o,
                int64_t B, int64_t S, int64_t H, int64_t D, float softmax_scale, int two_term,
                void* workspace, size_t workspace_bytes) {
@@ -405,13 +418,13 @@ int attn_setup(attn::Params& p, AttnWs& w, const void* q, const void* k, const v
   p.H = (int)H;
   p.S_pad = w.S_pad;
   p.softmax_scale = softmax_scale;
-  p.vperm = 1;
+  p.vperm = use_tc() ? 0 : 1;
   p.two_term = two_term ? 1 : 0;
   return KB200_OK;
 }
 
 int attn_quantize(const attn::Params& p, const AttnWs& w, cudaStream_t st) {
-  if (cudaMemsetAsync(p.amax, 0, (size_t)3 * p.B * p.H * 4, st) != cudaSuccess)
+  if (cudaMemsetAsync(p.amax, 0, (size_t)3 * p.B * p.H * 4 + 16, st) != cudaSuccess)
     return check_launch("attn_fp8 amax memset");
   attn::attn_amax_kernel<AD><<<dim3((unsigned)((p.S + 31) / 32), (unsigned)p.B), 256, 3 * p.H * 4, st>>>(p);
   if (int e = check_launch("attn_amax_kernel")) return e;
@@ -420,6 +433,7 @@ int attn_quantize(const attn::Params& p, const AttnWs& w, cudaStream_t st) {
 }
 
 int attn_attend(const attn::Params& p, const AttnWs& w, cudaStream_t st) {
+  if (!p.vperm) return attn::launch_attn_tc(p, reinterpret_cast<int*>(reinterpret_cast<char*>(p.amax) + (w.err - w.amax)), st);
   const size_t smem = sizeof(attn::MmaSmem<AD, ABM, ABN, ASTAGES>);
   auto kern = p.two_term ? attn::attn_fp8_mma_kernel<AD, ABM, ABN, ASTAGES, 2>
                          : attn::attn_fp8_mma_kernel<AD, ABM, ABN, ASTAGES, 1>;
@@ -455,4 +469,18 @@ extern "C" int kb200_attn_fp8_quantize(KB_ATTN_ARGS) {
 extern "C" int kb200_attn_fp8_attend(KB_ATTN_ARGS) {
   KB_ATTN_SETUP
   return attn_attend(p, w, st);
+}
+
+extern "C" int kb200_attn_fp8_status(const void* workspace, int64_t B, int64_t S, int64_t H, int two_term,
+                                     void* stream) {
+  if (!workspace || B <= 0 || S <= 0 || H <= 0) return set_error(KB200_ERR_INVALID, "attn_fp8_status: bad args");
+  const AttnWs w = attn_ws(B, S, H, two_term);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int code = 0;
+  if (cudaMemcpyAsync(&code, static_cast<const char*>(workspace) + w.err, sizeof(int), cudaMemcpyDeviceToHost, st) !=
+          cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)
+    return check_launch("attn_fp8_status");
+  if (code != 0) return set_error(KB200_ERR_TIMEOUT, "attn_fp8: a device-side wait gave up (site %d)", code);
+  return KB200_OK;
 }

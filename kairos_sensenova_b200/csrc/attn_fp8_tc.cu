@@ -1,0 +1,326 @@
+// attn_fp8_tc.cu -- FP8 (e4m3) flash-attention forward on 5th-generation
+// tensor cores (tcgen05 + TMEM + TMA), sm_100a.
+//
+// One CTA per (128-query tile, batch*head); keys in tiles of BN = 128.
+//   warp 4      : TMA producer (Q once; K, V^T (+ residual terms) per key tile
+//                 into a STAGES-deep ring)
+//   warp 5      : MMA issuer (one elected thread) and TMEM owner
+//                 S_j = Q K_j^T  -> TMEM S[j % 2]   (kind::f8f6f4, f32 accumulate)
+//                 O  += P_j V_j  -> TMEM O          (P_j from shared memory)
+//   warps 0..3  : softmax, one thread per query row / TMEM lane:
+//                 S row from TMEM -> running max (lazy rescale of O when the
+//                 max grows by more than TAU) -> P = 2^(s - m + SHIFT) as e4m3
+//                 into a 128B-swizzled smem tile -> final O / l -> bf16.
+// The MMA warp issues QK(j+1) before PV(j), so the tensor pipe works on the
+// next scores while the softmax warps process the current ones.
+//
+// Every mbarrier wait is bounded; a wait that gives up records an error code in
+// the workspace and the CTA skips the rest of its work, frees TMEM and exits.
+#include "attn_common.cuh"
+#include "kb200_internal.h"
+#include "tc_common.cuh"
+
+namespace kb {
+namespace attn {
+
+constexpr int TC_BM = 128, TC_BN = 128, TC_D = 128, TC_STAGES = 3;
+constexpr float TC_SHIFT = 6.f;   // P = 2^(s - m + SHIFT): keeps small probabilities out of e4m3 subnormals
+constexpr float TC_TAU = 2.5f;    // lazy-rescale threshold (log2 units); P <= 2^(SHIFT+TAU) < 448
+
+struct TcSmem {
+  uint8_t q[2][TC_BM * TC_D];                 // e4m3 q, residual term        (SW128, K-major)
+  uint8_t k[TC_STAGES][TC_BN * TC_D];         // e4m3 k tiles                  (SW128, K-major)
+  uint8_t v[TC_STAGES][2][TC_D * TC_BN];      // e4m3 v^T tiles + residual     (SW128, K-major over keys)
+  uint8_t p[2][TC_BM * TC_BN];                // e4m3 probabilities             (SW128, K-major over keys)
+  uint64_t q_full;
+  uint64_t kv_full[TC_STAGES], kv_empty[TC_STAGES];
+  uint64_t s_full[2], s_free[2], p_full[2], pv_done[2];
+  uint64_t o_done;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+struct TcMaps {
+  CUtensorMap q, qr, k, vt, vtr;
+};
+
+KB_DEVI void fail(TcSmem& sm, int* err, int code) {
+  sm.abort_flag = 1;
+  if (err) atomicCAS(err, 0, code);
+}
+
+template <int TT>
+__global__ void __launch_bounds__(192, 1) attn_fp8_tc_kernel(const __grid_constant__ TcMaps maps, Params p,
+                                                             int* err) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  // the swizzled tiles need 1024-byte alignment
+  TcSmem& sm = *reinterpret_cast<TcSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
+  const int q0 = blockIdx.x * TC_BM;
+  const int ntiles = (p.S + TC_BN - 1) / TC_BN;
+
+  if (tid == 0) {
+    tc::mbar_init(&sm.q_full, 1);
+    for (int s = 0; s < TC_STAGES; ++s) {
+      tc::mbar_init(&sm.kv_full[s], 1);
+      tc::mbar_init(&sm.kv_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(&sm.s_full[i], 1);
+      tc::mbar_init(&sm.s_free[i], 128);
+      tc::mbar_init(&sm.p_full[i], 128);
+      tc::mbar_init(&sm.pv_done[i], 1);
+    }
+    tc::mbar_init(&sm.o_done, 1);
+    sm.abort_flag = 0;
+    tc::fence_barrier_init();
+  }
+  if (warp == 5) {
+    tc::tmem_alloc(&sm.tmem_base, 512);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+  const uint32_t tS[2] = {tmem + 0, tmem + 128};
+  const uint32_t tO = tmem + 256;
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tc::prefetch_tmap(&maps.q);
+      tc::prefetch_tmap(&maps.k);
+      tc::prefetch_tmap(&maps.vt);
+      const int qrow = bh * p.S_pad + q0;
+      tc::mbar_expect_tx(&sm.q_full, TT * TC_BM * TC_D);
+      tc::tma_load_2d(sm.q[0], &maps.q, &sm.q_full, 0, qrow);
+      if (TT == 2) tc::tma_load_2d(sm.q[1], &maps.qr, &sm.q_full, 0, qrow);
+      for (int j = 0; j < ntiles; ++j) {
+        const int st = j % TC_STAGES, use = j / TC_STAGES;
+        if (j >= TC_STAGES && !tc::mbar_wait(&sm.kv_empty[st], (use - 1) & 1)) { fail(sm, err, 11); break; }
+        if (sm.abort_flag) break;
+        tc::mbar_expect_tx(&sm.kv_full[st], (1 + TT) * TC_BN * TC_D);
+        tc::tma_load_2d(sm.k[st], &maps.k, &sm.kv_full[st], 0, bh * p.S_pad + j * TC_BN);
+        tc::tma_load_2d(sm.v[st][0], &maps.vt, &sm.kv_full[st], j * TC_BN, bh * TC_D);
+        if (TT == 2) tc::tma_load_2d(sm.v[st][1], &maps.vtr, &sm.kv_full[st], j * TC_BN, bh * TC_D);
+      }
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t IDESC = tc::idesc_e4m3_f32(TC_BM, TC_BN);
+      bool ok = tc::mbar_wait(&sm.q_full, 0);
+      if (!ok) fail(sm, err, 12);
+      uint64_t dq[2] = {tc::sdesc_sw128_kmajor(sm.q[0]), tc::sdesc_sw128_kmajor(sm.q[1])};
+      auto issue_pv = [&](int jj) -> bool {
+        const int bb = jj & 1, u = jj >> 1, st = jj % TC_STAGES;
+        if (!tc::mbar_wait(&sm.p_full[bb], u & 1)) { fail(sm, err, 13); return false; }
+        tc::tc_fence_after();
+        const uint64_t dp = tc::sdesc_sw128_kmajor(sm.p[bb]);
+#pragma unroll
+        for (int t = 0; t < TT; ++t) {
+          const uint64_t dv = tc::sdesc_sw128_kmajor(sm.v[st][t]);
+#pragma unroll
+          for (int ks = 0; ks < TC_BN / 32; ++ks)
+            tc::mma_f8f6f4(tO, dp + 2 * ks, dv + 2 * ks, IDESC, (jj > 0 || t > 0 || ks > 0) ? 1u : 0u);
+        }
+        tc::tc_commit(&sm.pv_done[bb]);
+        tc::tc_commit(&sm.kv_empty[st]);
+        return true;
+      };
+      for (int j = 0; ok && j < ntiles; ++j) {
+        const int st = j % TC_STAGES, use = j / TC_STAGES;
+        const int bb = j & 1, u = j >> 1;
+        if (!tc::mbar_wait(&sm.kv_full[st], use & 1)) { fail(sm, err, 14); ok = false; break; }
+        if (j >= 2 && !tc::mbar_wait(&sm.s_free[bb], (u - 1) & 1)) { fail(sm, err, 15); ok = false; break; }
+        if (sm.abort_flag) { ok = false; break; }
+        tc::tc_fence_after();
+        const uint64_t dk = tc::sdesc_sw128_kmajor(sm.k[st]);
+#pragma unroll
+        for (int t = 0; t < TT; ++t)
+#pragma unroll
+          for (int ks = 0; ks < TC_D / 32; ++ks)
+            tc::mma_f8f6f4(tS[bb], dq[t] + 2 * ks, dk + 2 * ks, IDESC, (t > 0 || ks > 0) ? 1u : 0u);
+        tc::tc_commit(&sm.s_full[bb]);
+        if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
+      }
+      if (ok && ntiles > 0) ok = issue_pv(ntiles - 1);
+      tc::tc_commit(&sm.o_done);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax (warps 0..3)
+    const int r = tid;                                // query row within the tile == TMEM lane
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const float sq = scale_of(p.amax[(0 * p.B + b) * p.H + h]);
+    const float sk = scale_of(p.amax[(1 * p.B + b) * p.H + h]);
+    const float sv = scale_of(p.amax[(2 * p.B + b) * p.H + h]);
+    const float sl2 = sq * sk * p.softmax_scale * 1.4426950408889634f;   // raw score -> log2 units
+    float m_ref = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < ntiles; ++j) {
+      const int bb = j & 1, u = j >> 1;
+      if (!tc::mbar_wait(&sm.s_full[bb], u & 1)) { fail(sm, err, 21); ok = false; }
+      if (__any_sync(0xffffffffu, !ok || sm.abort_flag)) { ok = false; break; }
+      tc::tc_fence_after();
+      uint32_t s[TC_BN];
+#pragma unroll
+      for (int c = 0; c < TC_BN / 32; ++c) tc::tmem_ld32(tS[bb] + lane_off + c * 32, s + c * 32);
+      tc::tmem_wait_ld();
+      tc::tc_fence_before();
+      tc::mbar_arrive(&sm.s_free[bb]);
+      // mask keys past the end (last tile only)
+      const int kvalid = p.S - j * TC_BN;
+      if (kvalid < TC_BN) {
+#pragma unroll
+        for (int c = 0; c < TC_BN; ++c)
+          if (c >= kvalid) s[c] = __float_as_uint(-INFINITY);
+      }
+      float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < TC_BN; c += 4) {
+        mx0 = fmaxf(mx0, __uint_as_float(s[c]));
+        mx1 = fmaxf(mx1, __uint_as_float(s[c + 1]));
+        mx2 = fmaxf(mx2, __uint_as_float(s[c + 2]));
+        mx3 = fmaxf(mx3, __uint_as_float(s[c + 3]));
+      }
+      const float m_new = fmaxf(m_ref, fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2);
+      if (__any_sync(0xffffffffu, m_new > m_ref + TC_TAU)) {
+        const float alpha = exp2f(m_ref - m_new);     // 0 on the first tile
+        l *= alpha;
+        if (j > 0) {
+          // O holds the sum up to tile j-1: wait for PV(j-1), then rescale it in TMEM
+          const int pb = (j - 1) & 1, pu = (j - 1) >> 1;
+          if (!tc::mbar_wait(&sm.pv_done[pb], pu & 1)) { fail(sm, err, 22); ok = false; }
+          if (__any_sync(0xffffffffu, !ok)) { ok = false; break; }
+          tc::tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < TC_D / 32; ++c) {
+            uint32_t o[32];
+            tc::tmem_ld32(tO + lane_off + c * 32, o);
+            tc::tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            tc::tmem_st32(tO + lane_off + c * 32, o);
+          }
+          tc::tmem_wait_st();
+        }
+        m_ref = m_new;
+      }
+      // P tile buffer bb was last read by PV(j-2)
+      if (j >= 2) {
+        if (!tc::mbar_wait(&sm.pv_done[bb], (u - 1) & 1)) { fail(sm, err, 23); ok = false; }
+        if (__any_sync(0xffffffffu, !ok)) { ok = false; break; }
+      }
+      const float bias = TC_SHIFT - m_ref;
+      float ls = 0.f;
+      uint8_t* prow = sm.p[bb] + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+      for (int c16 = 0; c16 < TC_BN / 16; ++c16) {
+        uint32_t w4[4];
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          float e[4];
+#pragma unroll
+          for (int z = 0; z < 4; ++z) {
+            e[z] = exp2f(fmaf(__uint_as_float(s[c16 * 16 + q4 * 4 + z]), sl2, bias));
+            ls += e[z];
+          }
+          w4[q4] = f2_to_e4m3x2(e[0], e[1]) | (f2_to_e4m3x2(e[2], e[3]) << 16);
+        }
+        *reinterpret_cast<uint4*>(prow + ((c16 ^ (r & 7)) << 4)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+      }
+      l += ls;
+      tc::fence_proxy_async_smem();
+      tc::tc_fence_before();
+      tc::mbar_arrive(&sm.p_full[bb]);
+    }
+    // epilogue: O / l -> bf16 row
+    if (ok && __all_sync(0xffffffffu, tc::mbar_wait(&sm.o_done, 0))) {
+      tc::tc_fence_after();
+      const float f = sv / l;
+      const int row = q0 + r;
+      __nv_bfloat16* orow = p.o + ((size_t)b * p.S + row) * ((size_t)p.H * TC_D) + (size_t)h * TC_D;
+#pragma unroll
+      for (int c = 0; c < TC_D / 32; ++c) {
+        uint32_t o[32];
+        tc::tmem_ld32(tO + lane_off + c * 32, o);
+        tc::tmem_wait_ld();
+        if (row < p.S) {
+#pragma unroll
+          for (int z = 0; z < 32; z += 8) {
+            uint4 v;
+            v.x = pack_bf16(__uint_as_float(o[z + 0]) * f, __uint_as_float(o[z + 1]) * f);
+            v.y = pack_bf16(__uint_as_float(o[z + 2]) * f, __uint_as_float(o[z + 3]) * f);
+            v.z = pack_bf16(__uint_as_float(o[z + 4]) * f, __uint_as_float(o[z + 5]) * f);
+            v.w = pack_bf16(__uint_as_float(o[z + 6]) * f, __uint_as_float(o[z + 7]) * f);
+            *reinterpret_cast<uint4*>(orow + c * 32 + z) = v;
+          }
+        }
+      }
+    } else if (ok) {
+      fail(sm, err, 24);
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, 512);
+  }
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(f);
+  }
+  return fn;
+}
+
+// 2-D uint8 map over [rows, cols] (row stride `ld` bytes), 128 x 128 boxes, 128-byte swizzle.
+static int make_map(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, uint64_t ld) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return set_error(KB200_ERR_LAUNCH, "attn_fp8_tc: cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld};
+  cuuint32_t box[2] = {128, 128};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(KB200_ERR_LAUNCH, "attn_fp8_tc: tensor map encode failed (%d)", (int)r);
+  return KB200_OK;
+}
+
+int launch_attn_tc(const Params& p, int* err, cudaStream_t st) {
+  TcMaps maps;
+  const uint64_t rows_q = (uint64_t)p.B * p.H * p.S_pad, rows_v = (uint64_t)p.B * p.H * TC_D;
+  if (int e = make_map(&maps.q, p.q8, TC_D, rows_q, TC_D)) return e;
+  if (int e = make_map(&maps.k, p.k8, TC_D, rows_q, TC_D)) return e;
+  if (int e = make_map(&maps.vt, p.vt8, p.S_pad, rows_v, p.S_pad)) return e;
+  if (p.two_term) {
+    if (int e = make_map(&maps.qr, p.q8r, TC_D, rows_q, TC_D)) return e;
+    if (int e = make_map(&maps.vtr, p.vt8r, p.S_pad, rows_v, p.S_pad)) return e;
+  } else {
+    maps.qr = maps.q;
+    maps.vtr = maps.vt;
+  }
+  const size_t smem = sizeof(TcSmem) + 1024;
+  auto kern = p.two_term ? attn_fp8_tc_kernel<2> : attn_fp8_tc_kernel<1>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  kern<<<dim3(p.S_pad / TC_BM, (unsigned)(p.B * p.H)), 192, smem, st>>>(maps, p, err);
+  return check_launch("attn_fp8_tc_kernel");
+}
+
+}  // namespace attn
+}  // namespace kb
