@@ -343,7 +343,7 @@ struct AttnWs { size_t q8, k8, vt8, q8r, vt8r, amax, err, total; int S_pad; };
 
 AttnWs attn_ws(int64_t B, int64_t S, int64_t H, int two_term) {
   AttnWs w{};
-  w.S_pad = (int)((S + 127) / 128 * 128);
+  w.S_pad = (int)((S + 255) / 256 * 256);
   const size_t n = (size_t)B * H * w.S_pad * AD;
   size_t off = 0;
   auto take = [&](size_t bytes) { size_t o = off; off = align_up(off + bytes); return o; };

@@ -1,18 +1,19 @@
 // attn_fp8_tc.cu -- FP8 (e4m3) flash-attention forward on 5th-generation
 // tensor cores (tcgen05 + TMEM + TMA), sm_100a.
 //
-// One CTA per (128-query tile, batch*head); keys in tiles of BN = 128.
-//   warp 4      : TMA producer (Q once; K, V^T (+ residual terms) per key tile
+// One CTA per (two 128-query tiles, batch*head); keys in tiles of BN = 128.
+//   warp 8      : TMA producer (Q once; K, V^T (+ residual terms) per key tile
 //                 into a STAGES-deep ring)
-//   warp 5      : MMA issuer (one elected thread) and TMEM owner
-//                 S_j = Q K_j^T  -> TMEM S[j % 2]   (kind::f8f6f4, f32 accumulate)
-//                 O  += P_j V_j  -> TMEM O          (P_j from shared memory)
-//   warps 0..3  : softmax, one thread per query row / TMEM lane:
+//   warp 9      : MMA issuer (one elected thread) and TMEM owner
+//                 S_t = Q_t K_j^T  -> TMEM S[t]   (kind::f8f6f4, f32 accumulate)
+//                 O_t += P_t V_j   -> TMEM O[t]   (P_t from shared memory)
+//   warps 0..7  : softmax, warpgroup t for query tile t, one thread per row / TMEM lane:
 //                 S row from TMEM -> running max (lazy rescale of O when the
 //                 max grows by more than TAU) -> P = 2^(s - m + SHIFT) as e4m3
 //                 into a 128B-swizzled smem tile -> final O / l -> bf16.
-// The MMA warp issues QK(j+1) before PV(j), so the tensor pipe works on the
-// next scores while the softmax warps process the current ones.
+// The two query tiles ping-pong: while one warpgroup exponentiates its scores
+// the tensor pipe computes the other tile's scores or products, and the MMA
+// warp issues QK(j+1) before PV(j).
 //
 // Every mbarrier wait is bounded; a wait that gives up records an error code in
 // the workspace and the CTA skips the rest of its work, frees TMEM and exits.
@@ -23,18 +24,26 @@
 namespace kb {
 namespace attn {
 
-constexpr int TC_BM = 128, TC_BN = 128, TC_D = 128, TC_STAGES = 3;
+constexpr int TC_BM = 128, TC_BN = 128, TC_D = 128;
+constexpr int TC_QT = 2;          // query tiles per CTA (ping-pong between two softmax warpgroups)
 constexpr float TC_SHIFT = 6.f;   // P = 2^(s - m + SHIFT): keeps small probabilities out of e4m3 subnormals
 constexpr float TC_TAU = 2.5f;    // lazy-rescale threshold (log2 units); P <= 2^(SHIFT+TAU) < 448
 
+template <int TT>
+struct TcCfg {
+  static constexpr int STAGES = TT == 2 ? 2 : 3;   // K/V ring depth that fits in 227 KB
+};
+
+template <int TT>
 struct TcSmem {
-  uint8_t q[2][TC_BM * TC_D];                 // e4m3 q, residual term        (SW128, K-major)
-  uint8_t k[TC_STAGES][TC_BN * TC_D];         // e4m3 k tiles                  (SW128, K-major)
-  uint8_t v[TC_STAGES][2][TC_D * TC_BN];      // e4m3 v^T tiles + residual     (SW128, K-major over keys)
-  uint8_t p[2][TC_BM * TC_BN];                // e4m3 probabilities             (SW128, K-major over keys)
+  static constexpr int STAGES = TcCfg<TT>::STAGES;
+  uint8_t q[TC_QT][TT][TC_BM * TC_D];           // e4m3 q (+ residual term)        SW128 K-major
+  uint8_t p[TC_QT][TC_BM * TC_BN];              // e4m3 probabilities               SW128 K-major (keys)
+  uint8_t k[STAGES][TC_BN * TC_D];              // e4m3 k tiles                     SW128 K-major
+  uint8_t v[STAGES][TT][TC_D * TC_BN];          // e4m3 v^T tiles (+ residual)      SW128 K-major (keys)
   uint64_t q_full;
-  uint64_t kv_full[TC_STAGES], kv_empty[TC_STAGES];
-  uint64_t s_full[2], s_free[2], p_full[2], pv_done[2];
+  uint64_t kv_full[STAGES], kv_empty[STAGES];
+  uint64_t s_full[TC_QT], s_free[TC_QT], p_full[TC_QT], pv_done[TC_QT];
   uint64_t o_done;
   uint32_t tmem_base;
   int abort_flag;
@@ -44,29 +53,40 @@ struct TcMaps {
   CUtensorMap q, qr, k, vt, vtr;
 };
 
-KB_DEVI void fail(TcSmem& sm, int* err, int code) {
+template <class S>
+KB_DEVI void fail(S& sm, int* err, int code) {
   sm.abort_flag = 1;
   if (err) atomicCAS(err, 0, code);
 }
 
+KB_DEVI float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Block: warps 0-3 softmax for query tile 0, warps 4-7 for query tile 1,
+// warp 8 TMA producer, warp 9 MMA issuer + TMEM owner.
+// TMEM columns: S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512).
 template <int TT>
-__global__ void __launch_bounds__(192, 1) attn_fp8_tc_kernel(const __grid_constant__ TcMaps maps, Params p,
+__global__ void __launch_bounds__(320, 1) attn_fp8_tc_kernel(const __grid_constant__ TcMaps maps, Params p,
                                                              int* err) {
+  using SM = TcSmem<TT>;
+  constexpr int STAGES = SM::STAGES;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  // the swizzled tiles need 1024-byte alignment
-  TcSmem& sm = *reinterpret_cast<TcSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  SM& sm = *reinterpret_cast<SM*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
-  const int q0 = blockIdx.x * TC_BM;
+  const int q0 = blockIdx.x * (TC_QT * TC_BM);
   const int ntiles = (p.S + TC_BN - 1) / TC_BN;
 
   if (tid == 0) {
     tc::mbar_init(&sm.q_full, 1);
-    for (int s = 0; s < TC_STAGES; ++s) {
+    for (int s = 0; s < STAGES; ++s) {
       tc::mbar_init(&sm.kv_full[s], 1);
       tc::mbar_init(&sm.kv_empty[s], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < TC_QT; ++i) {
       tc::mbar_init(&sm.s_full[i], 1);
       tc::mbar_init(&sm.s_free[i], 128);
       tc::mbar_init(&sm.p_full[i], 128);
@@ -76,7 +96,7 @@ __global__ void __launch_bounds__(192, 1) attn_fp8_tc_kernel(const __grid_consta
     sm.abort_flag = 0;
     tc::fence_barrier_init();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tc::tmem_alloc(&sm.tmem_base, 512);
     tc::tmem_relinquish();
   }
@@ -84,168 +104,177 @@ __global__ void __launch_bounds__(192, 1) attn_fp8_tc_kernel(const __grid_consta
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
-  const uint32_t tS[2] = {tmem + 0, tmem + 128};
-  const uint32_t tO = tmem + 256;
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       tc::prefetch_tmap(&maps.q);
       tc::prefetch_tmap(&maps.k);
       tc::prefetch_tmap(&maps.vt);
-      const int qrow = bh * p.S_pad + q0;
-      tc::mbar_expect_tx(&sm.q_full, TT * TC_BM * TC_D);
-      tc::tma_load_2d(sm.q[0], &maps.q, &sm.q_full, 0, qrow);
-      if (TT == 2) tc::tma_load_2d(sm.q[1], &maps.qr, &sm.q_full, 0, qrow);
+      tc::mbar_expect_tx(&sm.q_full, TC_QT * TT * TC_BM * TC_D);
+      for (int qt = 0; qt < TC_QT; ++qt) {
+        const int qrow = bh * p.S_pad + q0 + qt * TC_BM;
+        tc::tma_load_2d(sm.q[qt][0], &maps.q, &sm.q_full, 0, qrow);
+        if (TT == 2) tc::tma_load_2d(sm.q[qt][TT - 1], &maps.qr, &sm.q_full, 0, qrow);
+      }
       for (int j = 0; j < ntiles; ++j) {
-        const int st = j % TC_STAGES, use = j / TC_STAGES;
-        if (j >= TC_STAGES && !tc::mbar_wait(&sm.kv_empty[st], (use - 1) & 1)) { fail(sm, err, 11); break; }
+        const int st = j % STAGES, use = j / STAGES;
+        if (j >= STAGES && !tc::mbar_wait(&sm.kv_empty[st], (use - 1) & 1)) { fail(sm, err, 11); break; }
         if (sm.abort_flag) break;
         tc::mbar_expect_tx(&sm.kv_full[st], (1 + TT) * TC_BN * TC_D);
         tc::tma_load_2d(sm.k[st], &maps.k, &sm.kv_full[st], 0, bh * p.S_pad + j * TC_BN);
         tc::tma_load_2d(sm.v[st][0], &maps.vt, &sm.kv_full[st], j * TC_BN, bh * TC_D);
-        if (TT == 2) tc::tma_load_2d(sm.v[st][1], &maps.vtr, &sm.kv_full[st], j * TC_BN, bh * TC_D);
+        if (TT == 2) tc::tma_load_2d(sm.v[st][TT - 1], &maps.vtr, &sm.kv_full[st], j * TC_BN, bh * TC_D);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t IDESC = tc::idesc_e4m3_f32(TC_BM, TC_BN);
       bool ok = tc::mbar_wait(&sm.q_full, 0);
       if (!ok) fail(sm, err, 12);
-      uint64_t dq[2] = {tc::sdesc_sw128_kmajor(sm.q[0]), tc::sdesc_sw128_kmajor(sm.q[1])};
-      auto issue_pv = [&](int jj) -> bool {
-        const int bb = jj & 1, u = jj >> 1, st = jj % TC_STAGES;
-        if (!tc::mbar_wait(&sm.p_full[bb], u & 1)) { fail(sm, err, 13); return false; }
+      auto issue_qk = [&](int qt, int j, int st) -> bool {
+        if (j >= 1 && !tc::mbar_wait(&sm.s_free[qt], (j - 1) & 1)) { fail(sm, err, 15); return false; }
         tc::tc_fence_after();
-        const uint64_t dp = tc::sdesc_sw128_kmajor(sm.p[bb]);
+        const uint64_t dk = tc::sdesc_sw128_kmajor(sm.k[st]);
+#pragma unroll
+        for (int t = 0; t < TT; ++t) {
+          const uint64_t dq = tc::sdesc_sw128_kmajor(sm.q[qt][t]);
+#pragma unroll
+          for (int ks = 0; ks < TC_D / 32; ++ks)
+            tc::mma_f8f6f4(tmem + qt * 128, dq + 2 * ks, dk + 2 * ks, IDESC, (t > 0 || ks > 0) ? 1u : 0u);
+        }
+        tc::tc_commit(&sm.s_full[qt]);
+        return true;
+      };
+      auto issue_pv = [&](int qt, int jj, int st) -> bool {
+        if (!tc::mbar_wait(&sm.p_full[qt], jj & 1)) { fail(sm, err, 13); return false; }
+        tc::tc_fence_after();
+        const uint64_t dp = tc::sdesc_sw128_kmajor(sm.p[qt]);
 #pragma unroll
         for (int t = 0; t < TT; ++t) {
           const uint64_t dv = tc::sdesc_sw128_kmajor(sm.v[st][t]);
 #pragma unroll
           for (int ks = 0; ks < TC_BN / 32; ++ks)
-            tc::mma_f8f6f4(tO, dp + 2 * ks, dv + 2 * ks, IDESC, (jj > 0 || t > 0 || ks > 0) ? 1u : 0u);
+            tc::mma_f8f6f4(tmem + 256 + qt * 128, dp + 2 * ks, dv + 2 * ks, IDESC,
+                           (jj > 0 || t > 0 || ks > 0) ? 1u : 0u);
         }
-        tc::tc_commit(&sm.pv_done[bb]);
-        tc::tc_commit(&sm.kv_empty[st]);
+        tc::tc_commit(&sm.pv_done[qt]);
         return true;
       };
       for (int j = 0; ok && j < ntiles; ++j) {
-        const int st = j % TC_STAGES, use = j / TC_STAGES;
-        const int bb = j & 1, u = j >> 1;
+        const int st = j % STAGES, use = j / STAGES;
         if (!tc::mbar_wait(&sm.kv_full[st], use & 1)) { fail(sm, err, 14); ok = false; break; }
-        if (j >= 2 && !tc::mbar_wait(&sm.s_free[bb], (u - 1) & 1)) { fail(sm, err, 15); ok = false; break; }
         if (sm.abort_flag) { ok = false; break; }
-        tc::tc_fence_after();
-        const uint64_t dk = tc::sdesc_sw128_kmajor(sm.k[st]);
-#pragma unroll
-        for (int t = 0; t < TT; ++t)
-#pragma unroll
-          for (int ks = 0; ks < TC_D / 32; ++ks)
-            tc::mma_f8f6f4(tS[bb], dq[t] + 2 * ks, dk + 2 * ks, IDESC, (t > 0 || ks > 0) ? 1u : 0u);
-        tc::tc_commit(&sm.s_full[bb]);
-        if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
+        if (!issue_qk(0, j, st) || !issue_qk(1, j, st)) { ok = false; break; }
+        if (j >= 1) {
+          const int sp = (j - 1) % STAGES;
+          if (!issue_pv(0, j - 1, sp) || !issue_pv(1, j - 1, sp)) { ok = false; break; }
+          tc::tc_commit(&sm.kv_empty[sp]);
+        }
       }
-      if (ok && ntiles > 0) ok = issue_pv(ntiles - 1);
+      if (ok && ntiles > 0) {
+        const int sp = (ntiles - 1) % STAGES;
+        ok = issue_pv(0, ntiles - 1, sp) && issue_pv(1, ntiles - 1, sp);
+      }
       tc::tc_commit(&sm.o_done);
     }
   } else {
-    // ------------------------------------------------------------ softmax (warps 0..3)
-    const int r = tid;                                // query row within the tile == TMEM lane
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    // ------------------------------------------------------------ softmax (warps 0..7)
+    const int qt = warp >> 2;                        // query tile of this warpgroup
+    const int r = tid & 127;                         // row in the tile == TMEM lane
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + qt * 128 + lane_off, tO = tmem + 256 + qt * 128 + lane_off;
     const float sq = scale_of(p.amax[(0 * p.B + b) * p.H + h]);
     const float sk = scale_of(p.amax[(1 * p.B + b) * p.H + h]);
     const float sv = scale_of(p.amax[(2 * p.B + b) * p.H + h]);
     const float sl2 = sq * sk * p.softmax_scale * 1.4426950408889634f;   // raw score -> log2 units
     float m_ref = -INFINITY, l = 0.f;
     bool ok = true;
+    uint8_t* prow = sm.p[qt] + (r >> 3) * 1024 + (r & 7) * 128;
     for (int j = 0; j < ntiles; ++j) {
-      const int bb = j & 1, u = j >> 1;
-      if (!tc::mbar_wait(&sm.s_full[bb], u & 1)) { fail(sm, err, 21); ok = false; }
+      if (!tc::mbar_wait(&sm.s_full[qt], j & 1)) { fail(sm, err, 21); ok = false; }
       if (__any_sync(0xffffffffu, !ok || sm.abort_flag)) { ok = false; break; }
       tc::tc_fence_after();
       uint32_t s[TC_BN];
 #pragma unroll
-      for (int c = 0; c < TC_BN / 32; ++c) tc::tmem_ld32(tS[bb] + lane_off + c * 32, s + c * 32);
+      for (int c = 0; c < TC_BN / 32; ++c) tc::tmem_ld32(tS + c * 32, s + c * 32);
       tc::tmem_wait_ld();
       tc::tc_fence_before();
-      tc::mbar_arrive(&sm.s_free[bb]);
-      // mask keys past the end (last tile only)
+      tc::mbar_arrive(&sm.s_free[qt]);
       const int kvalid = p.S - j * TC_BN;
       if (kvalid < TC_BN) {
 #pragma unroll
         for (int c = 0; c < TC_BN; ++c)
           if (c >= kvalid) s[c] = __float_as_uint(-INFINITY);
       }
-      float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+      float mx[8];
+#pragma unroll
+      for (int z = 0; z < 8; ++z) mx[z] = __uint_as_float(s[z]);
+#pragma unroll
+      for (int c = 8; c < TC_BN; c += 8)
+#pragma unroll
+        for (int z = 0; z < 8; ++z) mx[z] = fmaxf(mx[z], __uint_as_float(s[c + z]));
+      const float mraw = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                               fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      const float m_new = fmaxf(m_ref, mraw * sl2);
+      const bool rescale = __any_sync(0xffffffffu, m_new > m_ref + TC_TAU);
+      float alpha = 1.f;
+      if (rescale) {
+        alpha = ex2(m_ref - m_new);                  // 0 on the first tile
+        m_ref = m_new;
+      }
+      // exponentials (FFMA + MUFU), four partial row sums
+      const float bias = TC_SHIFT - m_ref;
+      float ls[4] = {0.f, 0.f, 0.f, 0.f};
+      uint32_t pk[TC_BN / 4];
 #pragma unroll
       for (int c = 0; c < TC_BN; c += 4) {
-        mx0 = fmaxf(mx0, __uint_as_float(s[c]));
-        mx1 = fmaxf(mx1, __uint_as_float(s[c + 1]));
-        mx2 = fmaxf(mx2, __uint_as_float(s[c + 2]));
-        mx3 = fmaxf(mx3, __uint_as_float(s[c + 3]));
+        float e[4];
+#pragma unroll
+        for (int z = 0; z < 4; ++z) {
+          e[z] = ex2(fmaf(__uint_as_float(s[c + z]), sl2, bias));
+          ls[z] += e[z];
+        }
+        pk[c / 4] = f2_to_e4m3x2(e[0], e[1]) | (f2_to_e4m3x2(e[2], e[3]) << 16);
       }
-      const float m_new = fmaxf(m_ref, fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2);
-      if (__any_sync(0xffffffffu, m_new > m_ref + TC_TAU)) {
-        const float alpha = exp2f(m_ref - m_new);     // 0 on the first tile
-        l *= alpha;
-        if (j > 0) {
-          // O holds the sum up to tile j-1: wait for PV(j-1), then rescale it in TMEM
-          const int pb = (j - 1) & 1, pu = (j - 1) >> 1;
-          if (!tc::mbar_wait(&sm.pv_done[pb], pu & 1)) { fail(sm, err, 22); ok = false; }
-          if (__any_sync(0xffffffffu, !ok)) { ok = false; break; }
-          tc::tc_fence_after();
+      l = l * alpha + ((ls[0] + ls[1]) + (ls[2] + ls[3]));
+      // PV(j-1) has finished reading the P buffer and adding into O
+      if (j >= 1) {
+        if (!tc::mbar_wait(&sm.pv_done[qt], (j - 1) & 1)) { fail(sm, err, 22); ok = false; }
+        if (__any_sync(0xffffffffu, !ok)) { ok = false; break; }
+        tc::tc_fence_after();
+        if (rescale) {
 #pragma unroll
           for (int c = 0; c < TC_D / 32; ++c) {
             uint32_t o[32];
-            tc::tmem_ld32(tO + lane_off + c * 32, o);
+            tc::tmem_ld32(tO + c * 32, o);
             tc::tmem_wait_ld();
 #pragma unroll
             for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-            tc::tmem_st32(tO + lane_off + c * 32, o);
+            tc::tmem_st32(tO + c * 32, o);
           }
           tc::tmem_wait_st();
         }
-        m_ref = m_new;
       }
-      // P tile buffer bb was last read by PV(j-2)
-      if (j >= 2) {
-        if (!tc::mbar_wait(&sm.pv_done[bb], (u - 1) & 1)) { fail(sm, err, 23); ok = false; }
-        if (__any_sync(0xffffffffu, !ok)) { ok = false; break; }
-      }
-      const float bias = TC_SHIFT - m_ref;
-      float ls = 0.f;
-      uint8_t* prow = sm.p[bb] + (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
-      for (int c16 = 0; c16 < TC_BN / 16; ++c16) {
-        uint32_t w4[4];
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          float e[4];
-#pragma unroll
-          for (int z = 0; z < 4; ++z) {
-            e[z] = exp2f(fmaf(__uint_as_float(s[c16 * 16 + q4 * 4 + z]), sl2, bias));
-            ls += e[z];
-          }
-          w4[q4] = f2_to_e4m3x2(e[0], e[1]) | (f2_to_e4m3x2(e[2], e[3]) << 16);
-        }
-        *reinterpret_cast<uint4*>(prow + ((c16 ^ (r & 7)) << 4)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
-      }
-      l += ls;
+      for (int c16 = 0; c16 < TC_BN / 16; ++c16)
+        *reinterpret_cast<uint4*>(prow + ((c16 ^ (r & 7)) << 4)) =
+            make_uint4(pk[4 * c16], pk[4 * c16 + 1], pk[4 * c16 + 2], pk[4 * c16 + 3]);
       tc::fence_proxy_async_smem();
       tc::tc_fence_before();
-      tc::mbar_arrive(&sm.p_full[bb]);
+      tc::mbar_arrive(&sm.p_full[qt]);
     }
     // epilogue: O / l -> bf16 row
     if (ok && __all_sync(0xffffffffu, tc::mbar_wait(&sm.o_done, 0))) {
       tc::tc_fence_after();
       const float f = sv / l;
-      const int row = q0 + r;
+      const int row = q0 + qt * TC_BM + r;
       __nv_bfloat16* orow = p.o + ((size_t)b * p.S + row) * ((size_t)p.H * TC_D) + (size_t)h * TC_D;
 #pragma unroll
       for (int c = 0; c < TC_D / 32; ++c) {
         uint32_t o[32];
-        tc::tmem_ld32(tO + lane_off + c * 32, o);
+        tc::tmem_ld32(tO + c * 32, o);
         tc::tmem_wait_ld();
         if (row < p.S) {
 #pragma unroll
@@ -265,7 +294,7 @@ __global__ void __launch_bounds__(192, 1) attn_fp8_tc_kernel(const __grid_consta
   }
   tc::tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc::tc_fence_after();
     tc::tmem_dealloc(tmem, 512);
   }
@@ -315,10 +344,11 @@ int launch_attn_tc(const Params& p, int* err, cudaStream_t st) {
     maps.qr = maps.q;
     maps.vtr = maps.vt;
   }
-  const size_t smem = sizeof(TcSmem) + 1024;
+  if (p.S_pad % (TC_QT * TC_BM)) return set_error(KB200_ERR_INVALID, "attn_fp8_tc: S_pad must be a multiple of 256");
+  const size_t smem = (p.two_term ? sizeof(TcSmem<2>) : sizeof(TcSmem<1>)) + 1024;
   auto kern = p.two_term ? attn_fp8_tc_kernel<2> : attn_fp8_tc_kernel<1>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  kern<<<dim3(p.S_pad / TC_BM, (unsigned)(p.B * p.H)), 192, smem, st>>>(maps, p, err);
+  kern<<<dim3(p.S_pad / (TC_QT * TC_BM), (unsigned)(p.B * p.H)), 320, smem, st>>>(maps, p, err);
   return check_launch("attn_fp8_tc_kernel");
 }
 
