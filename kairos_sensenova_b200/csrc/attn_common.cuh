@@ -22,6 +22,7 @@ struct Params {
   float softmax_scale;
   int vperm;     // 1: permute tokens inside 16-groups of vt8 for the mma.sync fragment order
   int two_term;  // 1: q and v carry a second e4m3 term (residual, same scale)
+  long long* trace;  // optional event timestamps of CTA (0,0) (builds with KB_ATTN_TRACE only)
 };
 
 KB_DEVI uint32_t f2_to_e4m3x2(float lo, float hi) {
