@@ -18,6 +18,8 @@
 // accumulations are fp32.  Tensor-core work uses mma.sync m16n8k16 bf16.
 #include "common.cuh"
 #include "kb200_internal.h"
+#include <type_traits>
+#include <cstring>
 
 namespace kb {
 namespace gdn {
@@ -50,6 +52,25 @@ struct Params {
   int l2norm;
 };
 
+// Warp-level 16x16 fp32 product: C = +-(A B [+ C]), row-major operands with
+// leading dimensions; lane l computes row l/2, columns 8*(l&1)..+8.  C must not
+// alias A or B.
+KB_DEVI void warp_mm16(float* C, int ldc, const float* A, int lda, const float* B, int ldb, bool acc,
+                       bool neg, int lane) {
+  const int r = lane >> 1, c0 = (lane & 1) * 8;
+  float o[8];
+#pragma unroll
+  for (int q = 0; q < 8; ++q) o[q] = acc ? C[r * ldc + c0 + q] : 0.f;
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    const float a = A[r * lda + k];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) o[q] = fmaf(a, B[k * ldb + c0 + q], o[q]);
+  }
+#pragma unroll
+  for (int q = 0; q < 8; ++q) C[r * ldc + c0 + q] = neg ? -o[q] : o[q];
+}
+
 // Locate chunk `c` (global index): sequence n, first token bos, in-sequence chunk it, length L.
 struct ChunkLoc { int n, it, bos, len; };
 KB_DEVI ChunkLoc locate_chunk(const Params& p, int c) {
@@ -75,14 +96,20 @@ KB_DEVI ChunkLoc locate_chunk(const Params& p, int c) {
 template <int K, int V>
 struct PrepSmem {
   static constexpr int LDK = K + 8, LDV = V + 8, LDA = BT + 1, LDI = BT + 8;
+  // The fp32 solve area (A, its inverse, merge temporaries) is first used to
+  // stage the q rows, and after the solve holds the bf16 inverse.
+  static constexpr int SOLVE_BYTES = (2 * BT * LDA + 4 * 256) * 4;
+  static constexpr int SCRATCH = SOLVE_BYTES > BT * LDK * 2 ? SOLVE_BYTES : BT * LDK * 2;
   __nv_bfloat16 ks[BT * LDK];   // k (normalised) then reused for beta e^g k
-  __nv_bfloat16 vb[BT * LDV];   // beta v
-  __nv_bfloat16 ai[BT * LDI];   // (I+A)^-1 in bf16
-  float af[BT * LDA];           // A (strictly lower), fp32
-  float xf[BT * LDA];           // (I+A)^-1, fp32
-  float yf[16 * 48];            // block-merge temporaries
+  __nv_bfloat16 vb[BT * LDV];   // v, then beta v
+  alignas(16) unsigned char scratch[SCRATCH];
   float gcs[BT];
   float bs[BT];
+  __device__ float* af() { return reinterpret_cast<float*>(scratch); }                 // A, strictly lower
+  __device__ float* xf() { return reinterpret_cast<float*>(scratch) + BT * LDA; }      // (I+A)^-1
+  __device__ float* yf() { return reinterpret_cast<float*>(scratch) + 2 * BT * LDA; }  // merge temporaries
+  __device__ __nv_bfloat16* qs() { return reinterpret_cast<__nv_bfloat16*>(scratch); } // staged q rows
+  __device__ __nv_bfloat16* ai() { return reinterpret_cast<__nv_bfloat16*>(scratch); } // bf16 inverse
 };
 
 template <int K, int V>
@@ -95,46 +122,24 @@ __global__ void __launch_bounds__(NTHREADS) gdn_prepare_kernel(Params p) {
   const ChunkLoc loc = locate_chunk(p, c);
   const int t0 = loc.bos + loc.it * BT, L = loc.len;
 
-  // ---- q/k rows: optional L2 norm (one warp per row), k kept in smem ----
-  constexpr int EPL = K / 32;  // elements per lane
-  for (int r = warp; r < BT; r += NTHREADS / 32) {
-    __nv_bfloat16* dst = sm.ks + r * S::LDK + lane * EPL;
-    if (r < L) {
-      const size_t off = ((size_t)(t0 + r) * H + h) * K + lane * EPL;
-      float x[EPL];
-#pragma unroll
-      for (int e = 0; e < EPL; ++e) x[e] = __bfloat162float(p.k[off + e]);
-      if (p.l2norm) {
-        float ss = 0.f;
-#pragma unroll
-        for (int e = 0; e < EPL; ++e) ss += x[e] * x[e];
-        ss = warp_sum(ss);
-        const float rstd = 1.0f / sqrtf(ss + 1e-6f);
-#pragma unroll
-        for (int e = 0; e < EPL; ++e) {
-          __nv_bfloat16 y = __float2bfloat16_rn(x[e] * rstd);
-          dst[e] = y;
-          p.kn[off + e] = y;
-        }
-        // q: same normalisation, written to the workspace for the output kernel
-        float y2[EPL];
-        float sq = 0.f;
-#pragma unroll
-        for (int e = 0; e < EPL; ++e) { y2[e] = __bfloat162float(p.q[off + e]); sq += y2[e] * y2[e]; }
-        sq = warp_sum(sq);
-        const float rq = 1.0f / sqrtf(sq + 1e-6f);
-#pragma unroll
-        for (int e = 0; e < EPL; ++e) p.qn[off + e] = __float2bfloat16_rn(y2[e] * rq);
-      } else {
-#pragma unroll
-        for (int e = 0; e < EPL; ++e) dst[e] = p.k[off + e];
-      }
-    } else {
-#pragma unroll
-      for (int e = 0; e < EPL; ++e) dst[e] = __float2bfloat16_rn(0.f);
+  // ---- stage the chunk: every k, q, v row with cp.async at once (one memory round trip) ----
+  {
+    constexpr int KV = K / 8, VV = V / 8;
+    for (int idx = tid; idx < BT * KV; idx += NTHREADS) {
+      const int r = idx / KV, cv = (idx % KV) * 8;
+      const bool ok = r < L;
+      const size_t off = ((size_t)(t0 + (ok ? r : 0)) * H + h) * K + cv;
+      cp_async16(sm.ks + r * S::LDK + cv, p.k + off, ok);
+      if (p.l2norm) cp_async16(sm.qs() + r * S::LDK + cv, p.q + off, ok);
     }
+    for (int idx = tid; idx < BT * VV; idx += NTHREADS) {
+      const int r = idx / VV, cv = (idx % VV) * 8;
+      const bool ok = r < L;
+      cp_async16(sm.vb + r * S::LDV + cv, p.v + ((size_t)(t0 + (ok ? r : 0)) * H + h) * V + cv, ok);
+    }
+    cp_async_commit();
   }
-  // ---- gate cumsum (warp 0) and beta ----
+  // ---- gate cumsum (warp 0) and beta (warp 1) while the copies fly ----
   if (warp == 0) {
     const int i0 = 2 * lane, i1 = 2 * lane + 1;
     float g0 = (i0 < L) ? p.g[(size_t)(t0 + i0) * H + h] : 0.f;
@@ -155,14 +160,50 @@ __global__ void __launch_bounds__(NTHREADS) gdn_prepare_kernel(Params p) {
     for (int i = lane; i < BT; i += 32)
       sm.bs[i] = (i < L) ? __bfloat162float(p.beta[(size_t)(t0 + i) * H + h]) : 0.f;
   }
-  // ---- beta v rows (bf16(v * beta)) ----
+  cp_async_wait<0>();
   __syncthreads();
+  // ---- optional L2 norm of q/k rows (l2norm.py:118-121: y = x / sqrt(sum x^2 + 1e-6),
+  // stored in bf16); one warp per row, one 8/16-byte vector per lane ----
+  if (p.l2norm) {
+    constexpr int EPL = K / 32;  // elements per lane (4 or 8)
+    using Vec = typename std::conditional<EPL == 4, uint2, uint4>::type;
+    for (int r = warp; r < L; r += NTHREADS / 32) {
+      Vec* kp = reinterpret_cast<Vec*>(sm.ks + r * S::LDK + lane * EPL);
+      const Vec kr = *kp;
+      const Vec qr = *reinterpret_cast<const Vec*>(sm.qs() + r * S::LDK + lane * EPL);
+      const __nv_bfloat16* ke = reinterpret_cast<const __nv_bfloat16*>(&kr);
+      const __nv_bfloat16* qe = reinterpret_cast<const __nv_bfloat16*>(&qr);
+      float sk = 0.f, sq = 0.f;
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) {
+        const float xk = __bfloat162float(ke[e]), xq = __bfloat162float(qe[e]);
+        sk += xk * xk;
+        sq += xq * xq;
+      }
+      sk = warp_sum(sk);
+      sq = warp_sum(sq);
+      const float rk = 1.0f / sqrtf(sk + 1e-6f), rq = 1.0f / sqrtf(sq + 1e-6f);
+      Vec ko, qo;
+      uint32_t* ko32 = reinterpret_cast<uint32_t*>(&ko);
+      uint32_t* qo32 = reinterpret_cast<uint32_t*>(&qo);
+#pragma unroll
+      for (int e = 0; e < EPL; e += 2) {
+        ko32[e / 2] = pack_bf16(__bfloat162float(ke[e]) * rk, __bfloat162float(ke[e + 1]) * rk);
+        qo32[e / 2] = pack_bf16(__bfloat162float(qe[e]) * rq, __bfloat162float(qe[e + 1]) * rq);
+      }
+      *kp = ko;
+      const size_t off = ((size_t)(t0 + r) * H + h) * K + lane * EPL;
+      *reinterpret_cast<Vec*>(p.kn + off) = ko;
+      *reinterpret_cast<Vec*>(p.qn + off) = qo;
+    }
+  }
+  // ---- beta v in place (bf16(v * beta), wy_fast.py:67) ----
   {
-    constexpr int VPR = V / 8;  // 16-byte vectors per row
+    constexpr int VPR = V / 8;
     for (int idx = tid; idx < BT * VPR; idx += NTHREADS) {
       const int r = idx / VPR, cv = (idx % VPR) * 8;
-      uint4 raw = make_uint4(0, 0, 0, 0);
-      if (r < L) raw = *reinterpret_cast<const uint4*>(p.v + ((size_t)(t0 + r) * H + h) * V + cv);
+      uint4* ptr = reinterpret_cast<uint4*>(sm.vb + r * S::LDV + cv);
+      const uint4 raw = *ptr;
       const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
       const float b = sm.bs[r];
       uint4 outv;
@@ -170,9 +211,10 @@ __global__ void __launch_bounds__(NTHREADS) gdn_prepare_kernel(Params p) {
 #pragma unroll
       for (int j = 0; j < 4; ++j)
         ov[j] = pack_bf16(__bfloat162float(e[2 * j]) * b, __bfloat162float(e[2 * j + 1]) * b);
-      *reinterpret_cast<uint4*>(sm.vb + r * S::LDV + cv) = outv;
+      *ptr = outv;
     }
   }
+  __syncthreads();
   // ---- A = beta_i e^{g_i - g_j} <k_i, k_j>, strictly lower (warp w: rows 16w..16w+15) ----
   {
     float acc[8][4];
@@ -201,7 +243,7 @@ __global__ void __launch_bounds__(NTHREADS) gdn_prepare_kernel(Params p) {
         const int j = n * 8 + 2 * t4 + (e & 1);
         float val = 0.f;
         if (i > j && i < L) val = acc[n][e] * __expf(sm.gcs[i] - sm.gcs[j]) * sm.bs[i];
-        sm.af[i * S::LDA + j] = val;
+        sm.af()[i * S::LDA + j] = val;
       }
   }
   __syncthreads();
@@ -233,42 +275,63 @@ __global__ void __launch_bounds__(NTHREADS) gdn_prepare_kernel(Params p) {
     for (int r = 1; r < 16; ++r) {
       float s = 0.f;
 #pragma unroll
-      for (int m = 0; m < r; ++m) s += sm.af[(base + r) * S::LDA + base + m] * x[m];
+      for (int m = 0; m < r; ++m) s += sm.af()[(base + r) * S::LDA + base + m] * x[m];
       if (r > col) x[r] = -s;
     }
 #pragma unroll
-    for (int r = 0; r < 16; ++r) sm.xf[(base + r) * S::LDA + base + col] = x[r];
+    for (int r = 0; r < 16; ++r) sm.xf()[(base + r) * S::LDA + base + col] = x[r];
   }
   // zero the strictly-upper blocks
   for (int idx = tid; idx < BT * BT; idx += NTHREADS) {
     const int r = idx >> 6, cc = idx & 63;
-    if ((cc >> 4) > (r >> 4)) sm.xf[r * S::LDA + cc] = 0.f;
+    if ((cc >> 4) > (r >> 4)) sm.xf()[r * S::LDA + cc] = 0.f;
   }
   __syncthreads();
-  // ---- block merge: X_ij = -D_i sum_{m=j}^{i-1} A_im X_mj, block rows in order ----
-  for (int bi = 1; bi < 4; ++bi) {
-    const int ncols = bi * 16;  // columns j-blocks 0..bi-1
-    for (int idx = tid; idx < 16 * ncols; idx += NTHREADS) {
-      const int r = idx / ncols, cc = idx % ncols;
-      const int jb = cc >> 4;
-      float s = 0.f;
-      for (int m = jb * 16; m < bi * 16; ++m)
-        s += sm.af[(bi * 16 + r) * S::LDA + m] * sm.xf[m * S::LDA + cc];
-      sm.yf[r * 48 + cc] = s;
+  // ---- block merge (solve_tril.py:265-290, fp32 like its 'ieee' dots):
+  //   X21 = -D2 A21 D1, X32 = -D3 A32 D2, X43 = -D4 A43 D3,
+  //   X31 = -D3 (A31 D1 + A32 X21), X42 = -D4 (A42 D2 + A43 X32),
+  //   X41 = -D4 (A41 D1 + A42 X21 + A43 X31)      (block indices 1-based)
+  // as warp-level 16x16 fp32 products, three warps in parallel per level ----
+  {
+    auto Ab = [&](int i, int j) { return sm.af() + (16 * i) * S::LDA + 16 * j; };
+    auto Xb = [&](int i, int j) { return sm.xf() + (16 * i) * S::LDA + 16 * j; };
+    float* T = sm.yf() + warp * 256;
+    if (warp < 3) {
+      const int i = warp + 1;
+      warp_mm16(T, 16, Ab(i, i - 1), S::LDA, Xb(i - 1, i - 1), S::LDA, false, false, lane);
+      __syncwarp();
+      warp_mm16(Xb(i, i - 1), S::LDA, Xb(i, i), S::LDA, T, 16, false, true, lane);
     }
     __syncthreads();
-    for (int idx = tid; idx < 16 * ncols; idx += NTHREADS) {
-      const int r = idx / ncols, cc = idx % ncols;
-      float s = 0.f;
-      for (int m = 0; m <= r; ++m)
-        s += sm.xf[(bi * 16 + r) * S::LDA + bi * 16 + m] * sm.yf[m * 48 + cc];
-      sm.xf[(bi * 16 + r) * S::LDA + cc] = -s;
+    if (warp == 0) {
+      warp_mm16(T, 16, Ab(2, 0), S::LDA, Xb(0, 0), S::LDA, false, false, lane);
+      __syncwarp();
+      warp_mm16(T, 16, Ab(2, 1), S::LDA, Xb(1, 0), S::LDA, true, false, lane);
+      __syncwarp();
+      warp_mm16(Xb(2, 0), S::LDA, Xb(2, 2), S::LDA, T, 16, false, true, lane);
+    } else if (warp == 1) {
+      warp_mm16(T, 16, Ab(3, 1), S::LDA, Xb(1, 1), S::LDA, false, false, lane);
+      __syncwarp();
+      warp_mm16(T, 16, Ab(3, 2), S::LDA, Xb(2, 1), S::LDA, true, false, lane);
+      __syncwarp();
+      warp_mm16(Xb(3, 1), S::LDA, Xb(3, 3), S::LDA, T, 16, false, true, lane);
+    } else if (warp == 2) {
+      warp_mm16(T, 16, Ab(3, 0), S::LDA, Xb(0, 0), S::LDA, false, false, lane);
+      __syncwarp();
+      warp_mm16(T, 16, Ab(3, 1), S::LDA, Xb(1, 0), S::LDA, true, false, lane);
+    }
+    __syncthreads();
+    if (warp == 0) {
+      float* T2 = sm.yf() + 2 * 256;
+      warp_mm16(T2, 16, Ab(3, 2), S::LDA, Xb(2, 0), S::LDA, true, false, lane);
+      __syncwarp();
+      warp_mm16(Xb(3, 0), S::LDA, Xb(3, 3), S::LDA, T2, 16, false, true, lane);
     }
     __syncthreads();
   }
   for (int idx = tid; idx < BT * BT; idx += NTHREADS) {
     const int r = idx >> 6, cc = idx & 63;
-    sm.ai[r * S::LDI + cc] = __float2bfloat16_rn(sm.xf[r * S::LDA + cc]);
+    sm.ai()[r * S::LDI + cc] = __float2bfloat16_rn(sm.xf()[r * S::LDA + cc]);
   }
   __syncthreads();
   // ---- u = Ai (beta v), w = Ai (beta e^g k), 64-column slabs ----
@@ -276,7 +339,7 @@ __global__ void __launch_bounds__(NTHREADS) gdn_prepare_kernel(Params p) {
     const int g8 = lane >> 2, t4 = lane & 3;
     uint32_t afr[4][4];
 #pragma unroll
-    for (int ks = 0; ks < 4; ++ks) load_a_rowmajor(afr[ks], sm.ai, S::LDI, warp * 16, ks * 16, lane);
+    for (int ks = 0; ks < 4; ++ks) load_a_rowmajor(afr[ks], sm.ai(), S::LDI, warp * 16, ks * 16, lane);
     const int r0 = warp * 16 + g8, r1 = r0 + 8;
     for (int slab = 0; slab < (V + K) / 64; ++slab) {
       const bool isu = slab < V / 64;
@@ -314,45 +377,56 @@ __global__ void __launch_bounds__(NTHREADS) gdn_prepare_kernel(Params p) {
 }
 
 // ---------------------------------------------------------------------------
-// Kernel 2: sequential state pass.  Grid (V / BV, N * H); 4 warps.
-// Warp w owns state rows [w*K/4, (w+1)*K/4) x BV columns in fp32 registers.
-// Per chunk: w, k, u tiles are double-buffered in shared memory (cp.async).
+// Kernel 2: sequential state pass.  Grid (V / BV, N * H); 8 warps.
+//   v_new = u - w h   : warp w computes rows 16 (w & 3).., columns BV/2 (w >> 2)..
+//   h <- e^{g_last} h + k^T vg : warp w owns state rows [w K/8, (w+1) K/8)
+// The next chunk's w, k, u and g tiles stream in with cp.async while the
+// current one is processed; the bf16 state snapshot and the gated v_new are
+// double-buffered, so each step needs two block barriers.
 // ---------------------------------------------------------------------------
+constexpr int STATE_THREADS = 256;
+
 template <int K, int BV>
 struct StateSmem {
   static constexpr int LDK = K + 8, LDV = BV + 8;
   __nv_bfloat16 ws[2][BT * LDK];
   __nv_bfloat16 ks[2][BT * LDK];
   __nv_bfloat16 us[2][BT * LDV];
-  __nv_bfloat16 hb[K * LDV];      // bf16 snapshot of the state (B operand of w h)
-  __nv_bfloat16 vg[BT * LDV];     // gated v_new (B operand of k^T v)
+  __nv_bfloat16 hb[2][K * LDV];   // bf16 snapshot of the state (B operand of w h)
+  __nv_bfloat16 vg[2][BT * LDV];  // gated v_new (B operand of k^T v)
   float gcs[2][BT];
 };
+
+KB_DEVI void cp_async4(void* smem, const void* gmem, bool pred) {
+  int n = pred ? 4 : 0;
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(smem_u32(smem)), "l"(gmem), "r"(n));
+}
 
 template <int K, int BV>
 KB_DEVI void state_issue_loads(StateSmem<K, BV>& sm, int buf, const Params& p, int t0, int L,
                                int h, int v0, int V, int tid) {
   const int H = p.H;
   constexpr int KV = K / 8, VV = BV / 8;
-  for (int idx = tid; idx < BT * KV; idx += NTHREADS) {
+  for (int idx = tid; idx < BT * KV; idx += STATE_THREADS) {
     const int r = idx / KV, cv = (idx % KV) * 8;
     const bool ok = r < L;
     const size_t off = ((size_t)(t0 + (ok ? r : 0)) * H + h) * K + cv;
     cp_async16(&sm.ws[buf][r * StateSmem<K, BV>::LDK + cv], p.w + off, ok);
     cp_async16(&sm.ks[buf][r * StateSmem<K, BV>::LDK + cv], p.kn + off, ok);
   }
-  for (int idx = tid; idx < BT * VV; idx += NTHREADS) {
+  for (int idx = tid; idx < BT * VV; idx += STATE_THREADS) {
     const int r = idx / VV, cv = (idx % VV) * 8;
     const bool ok = r < L;
     const size_t off = ((size_t)(t0 + (ok ? r : 0)) * H + h) * V + v0 + cv;
     cp_async16(&sm.us[buf][r * StateSmem<K, BV>::LDV + cv], p.u + off, ok);
   }
-  if (tid < BT) sm.gcs[buf][tid] = (tid < L) ? p.gc[(size_t)(t0 + tid) * H + h] : 0.f;
+  if (tid < BT) cp_async4(&sm.gcs[buf][tid], p.gc + (size_t)(t0 + (tid < L ? tid : 0)) * H + h, tid < L);
   cp_async_commit();
 }
 
 template <int K, int V, int BV>
-__global__ void __launch_bounds__(NTHREADS) gdn_state_kernel(Params p) {
+__global__ void __launch_bounds__(STATE_THREADS) gdn_state_kernel(Params p) {
+  static_assert(BV == 32, "state kernel tiles assume BV = 32");
   extern __shared__ __align__(128) unsigned char smem_raw[];
   using S = StateSmem<K, BV>;
   S& sm = *reinterpret_cast<S*>(smem_raw);
@@ -371,9 +445,10 @@ __global__ void __launch_bounds__(NTHREADS) gdn_state_kernel(Params p) {
     cbase = n * p.NT;
   }
   const int NTn = (Tn + BT - 1) / BT;
-  constexpr int RW = K / 4;        // state rows per warp
+  constexpr int RW = K / 8;        // state rows per warp
   constexpr int MT = RW / 16;      // m-tiles per warp
-  constexpr int NB = BV / 8;       // n-tiles
+  constexpr int NB = BV / 8;       // n-tiles of the state
+  const int m0 = warp * RW;
   float hacc[MT][NB][4];
 #pragma unroll
   for (int m = 0; m < MT; ++m)
@@ -381,27 +456,29 @@ __global__ void __launch_bounds__(NTHREADS) gdn_state_kernel(Params p) {
     for (int nn = 0; nn < NB; ++nn)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const int r = warp * RW + m * 16 + g8 + ((e >> 1) << 3);
+        const int r = m0 + m * 16 + g8 + ((e >> 1) << 3);
         const int cc = v0 + nn * 8 + 2 * t4 + (e & 1);
         hacc[m][nn][e] = p.h0 ? p.h0[((size_t)nh * K + r) * V + cc] : 0.f;
       }
   if (NTn > 0) state_issue_loads<K, BV>(sm, 0, p, bos, min(BT, Tn), h, v0, V, tid);
+  const int rg = warp & 3, c0 = (warp >> 2) * (BV / 2);
 
   for (int it = 0; it < NTn; ++it) {
     const int buf = it & 1;
     const int t0 = bos + it * BT, L = min(BT, Tn - it * BT);
     // (a) snapshot: bf16 state -> smem operand and -> global h[chunk]
     __nv_bfloat16* hg = p.hs + ((size_t)(cbase + it) * H + h) * K * V;
+    __nv_bfloat16* hb = sm.hb[buf];
 #pragma unroll
     for (int m = 0; m < MT; ++m)
 #pragma unroll
       for (int nn = 0; nn < NB; ++nn) {
-        const int r = warp * RW + m * 16 + g8;
+        const int r = m0 + m * 16 + g8;
         const int cc = nn * 8 + 2 * t4;
         const uint32_t lo = pack_bf16(hacc[m][nn][0], hacc[m][nn][1]);
         const uint32_t hi = pack_bf16(hacc[m][nn][2], hacc[m][nn][3]);
-        *reinterpret_cast<uint32_t*>(&sm.hb[r * S::LDV + cc]) = lo;
-        *reinterpret_cast<uint32_t*>(&sm.hb[(r + 8) * S::LDV + cc]) = hi;
+        *reinterpret_cast<uint32_t*>(&hb[r * S::LDV + cc]) = lo;
+        *reinterpret_cast<uint32_t*>(&hb[(r + 8) * S::LDV + cc]) = hi;
         *reinterpret_cast<uint32_t*>(hg + (size_t)r * V + v0 + cc) = lo;
         *reinterpret_cast<uint32_t*>(hg + (size_t)(r + 8) * V + v0 + cc) = hi;
       }
@@ -409,42 +486,45 @@ __global__ void __launch_bounds__(NTHREADS) gdn_state_kernel(Params p) {
     __syncthreads();
     if (it + 1 < NTn)
       state_issue_loads<K, BV>(sm, buf ^ 1, p, t0 + BT, min(BT, Tn - (it + 1) * BT), h, v0, V, tid);
-    // (b) v_new = u - w h   (warp w: rows 16w..16w+15)
+    // (b) v_new = u - w h   (rows 16 rg.., columns c0..c0+BV/2); two accumulator sets halve the chain
     const float glast = sm.gcs[buf][L - 1];
+    __nv_bfloat16* vg = sm.vg[buf];
     {
-      float acc[NB][4];
+      float acc0[2][4], acc1[2][4];
 #pragma unroll
-      for (int nn = 0; nn < NB; ++nn)
+      for (int nn = 0; nn < 2; ++nn)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) acc[nn][e] = 0.f;
-#pragma unroll 4
-      for (int kk = 0; kk < K; kk += 16) {
-        uint32_t a[4];
-        load_a_rowmajor(a, sm.ws[buf], S::LDK, warp * 16, kk, lane);
+        for (int e = 0; e < 4; ++e) acc0[nn][e] = acc1[nn][e] = 0.f;
 #pragma unroll
-        for (int n0 = 0; n0 < BV; n0 += 16) {
-          uint32_t b[4];
-          load_b_kmajor_rows_x2n(b, sm.hb, S::LDV, kk, n0, lane);
-          mma_bf16(acc[n0 / 8], a, b);
-          mma_bf16(acc[n0 / 8 + 1], a, b + 2);
-        }
+      for (int kk = 0; kk < K; kk += 32) {
+        uint32_t a0[4], a1[4], b0[4], b1[4];
+        load_a_rowmajor(a0, sm.ws[buf], S::LDK, rg * 16, kk, lane);
+        load_b_kmajor_rows_x2n(b0, hb, S::LDV, kk, c0, lane);
+        load_a_rowmajor(a1, sm.ws[buf], S::LDK, rg * 16, kk + 16, lane);
+        load_b_kmajor_rows_x2n(b1, hb, S::LDV, kk + 16, c0, lane);
+        mma_bf16(acc0[0], a0, b0);
+        mma_bf16(acc0[1], a0, b0 + 2);
+        mma_bf16(acc1[0], a1, b1);
+        mma_bf16(acc1[1], a1, b1 + 2);
       }
-      const int r0 = warp * 16 + g8, r1 = r0 + 8;
+      const int r0 = rg * 16 + g8, r1 = r0 + 8;
       const float e0 = (r0 < L) ? __expf(glast - sm.gcs[buf][r0]) : 0.f;
       const float e1 = (r1 < L) ? __expf(glast - sm.gcs[buf][r1]) : 0.f;
 #pragma unroll
-      for (int nn = 0; nn < NB; ++nn) {
-        const int cc = nn * 8 + 2 * t4;
+      for (int nn = 0; nn < 2; ++nn) {
+        const int cc = c0 + nn * 8 + 2 * t4;
         const __nv_bfloat162 u0 = *reinterpret_cast<const __nv_bfloat162*>(&sm.us[buf][r0 * S::LDV + cc]);
         const __nv_bfloat162 u1 = *reinterpret_cast<const __nv_bfloat162*>(&sm.us[buf][r1 * S::LDV + cc]);
-        const float a0 = __low2float(u0) - acc[nn][0], a1 = __high2float(u0) - acc[nn][1];
-        const float a2 = __low2float(u1) - acc[nn][2], a3 = __high2float(u1) - acc[nn][3];
+        const float a0 = __low2float(u0) - (acc0[nn][0] + acc1[nn][0]);
+        const float a1 = __high2float(u0) - (acc0[nn][1] + acc1[nn][1]);
+        const float a2 = __low2float(u1) - (acc0[nn][2] + acc1[nn][2]);
+        const float a3 = __high2float(u1) - (acc0[nn][3] + acc1[nn][3]);
         if (r0 < L)
           *reinterpret_cast<uint32_t*>(p.vnew + ((size_t)(t0 + r0) * H + h) * V + v0 + cc) = pack_bf16(a0, a1);
         if (r1 < L)
           *reinterpret_cast<uint32_t*>(p.vnew + ((size_t)(t0 + r1) * H + h) * V + v0 + cc) = pack_bf16(a2, a3);
-        *reinterpret_cast<uint32_t*>(&sm.vg[r0 * S::LDV + cc]) = pack_bf16(a0 * e0, a1 * e0);
-        *reinterpret_cast<uint32_t*>(&sm.vg[r1 * S::LDV + cc]) = pack_bf16(a2 * e1, a3 * e1);
+        *reinterpret_cast<uint32_t*>(&vg[r0 * S::LDV + cc]) = pack_bf16(a0 * e0, a1 * e0);
+        *reinterpret_cast<uint32_t*>(&vg[r1 * S::LDV + cc]) = pack_bf16(a2 * e1, a3 * e1);
       }
     }
     __syncthreads();
@@ -462,18 +542,17 @@ __global__ void __launch_bounds__(NTHREADS) gdn_state_kernel(Params p) {
 #pragma unroll
         for (int m = 0; m < MT; ++m) {
           uint32_t a[4];
-          load_a_transposed(a, sm.ks[buf], S::LDK, warp * RW + m * 16, kk, lane);
+          load_a_transposed(a, sm.ks[buf], S::LDK, m0 + m * 16, kk, lane);
 #pragma unroll
           for (int n0 = 0; n0 < BV; n0 += 16) {
             uint32_t b[4];
-            load_b_kmajor_rows_x2n(b, sm.vg, S::LDV, kk, n0, lane);
+            load_b_kmajor_rows_x2n(b, vg, S::LDV, kk, n0, lane);
             mma_bf16(hacc[m][n0 / 8], a, b);
             mma_bf16(hacc[m][n0 / 8 + 1], a, b + 2);
           }
         }
       }
     }
-    __syncthreads();
   }
   if (p.ht) {
 #pragma unroll
@@ -482,7 +561,7 @@ __global__ void __launch_bounds__(NTHREADS) gdn_state_kernel(Params p) {
       for (int nn = 0; nn < NB; ++nn)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const int r = warp * RW + m * 16 + g8 + ((e >> 1) << 3);
+          const int r = m0 + m * 16 + g8 + ((e >> 1) << 3);
           const int cc = v0 + nn * 8 + 2 * t4 + (e & 1);
           p.ht[((size_t)nh * K + r) * V + cc] = hacc[m][nn][e];
         }
@@ -702,7 +781,7 @@ int launch(const KB200GdnArgs* a, const WsLayout& L, char* ws, cudaStream_t st) 
   }
   const size_t s2 = sizeof(gdn::StateSmem<K, BV>);
   cudaFuncSetAttribute(gdn::gdn_state_kernel<K, V, BV>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s2);
-  gdn::gdn_state_kernel<K, V, BV><<<dim3(V / BV, (unsigned)(a->N * H)), gdn::NTHREADS, s2, st>>>(p);
+  gdn::gdn_state_kernel<K, V, BV><<<dim3(V / BV, (unsigned)(a->N * H)), gdn::STATE_THREADS, s2, st>>>(p);
   if (int e = check_launch("gdn_state_kernel")) return e;
   if (nchunks > 0) {
     const size_t s3 = sizeof(gdn::OutSmem<K, BVO>);
