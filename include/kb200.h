@@ -94,7 +94,9 @@ int kb200_gdn_chunk_fwd_noalloc(const KB200GdnArgs* a, void* stream);
  *   kairos/modules/dits/kairos_dit.py:367-373 (module)
  *   kairos/modules/dits/kairos_dit.py:232-277 (flash_attention dispatcher;
  *   non-causal, no mask, softmax scale D^-1/2 as in F.scaled_dot_product_attention)
- * q, k, v, o: [B, S, H*D] bf16, D = 128.
+ * q, k, v: [B, S, H*D] bf16 rows, `row_stride` elements apart (0 = H*D, i.e.
+ * contiguous; larger when q/k/v are column slices of one fused projection);
+ * o: [B, S, H*D] bf16 contiguous; D = 128.
  * two_term = 1 adds a second e4m3 term (the rounding residual, same per-head
  * scale) to q and to v, which doubles the tensor-core work and lifts the
  * cosine similarity to the bf16 reference from ~0.9986 to ~0.9993 on
@@ -102,18 +104,19 @@ int kb200_gdn_chunk_fwd_noalloc(const KB200GdnArgs* a, void* stream);
  * --------------------------------------------------------------------- */
 size_t kb200_attn_fp8_workspace_size(int64_t B, int64_t S, int64_t H, int64_t D, int two_term);
 int kb200_attn_fp8_fwd(const void* q, const void* k, const void* v, void* o, int64_t B, int64_t S,
-                       int64_t H, int64_t D, float softmax_scale, int two_term, void* workspace,
-                       size_t workspace_bytes, void* stream);
+                       int64_t H, int64_t D, int64_t row_stride, float softmax_scale, int two_term,
+                       void* workspace, size_t workspace_bytes, void* stream);
 /* The two halves of kb200_attn_fp8_fwd, for callers that time or overlap them
  * separately: _quantize fills the workspace (amax, e4m3 q/k/v^T), _attend reads
  * it and writes o.  Same arguments; _attend must follow a _quantize of the
  * same inputs into the same workspace on the same stream. */
 int kb200_attn_fp8_quantize(const void* q, const void* k, const void* v, void* o, int64_t B,
-                            int64_t S, int64_t H, int64_t D, float softmax_scale, int two_term,
-                            void* workspace, size_t workspace_bytes, void* stream);
+                            int64_t S, int64_t H, int64_t D, int64_t row_stride,
+                            float softmax_scale, int two_term, void* workspace,
+                            size_t workspace_bytes, void* stream);
 int kb200_attn_fp8_attend(const void* q, const void* k, const void* v, void* o, int64_t B,
-                          int64_t S, int64_t H, int64_t D, float softmax_scale, int two_term,
-                          void* workspace, size_t workspace_bytes, void* stream);
+                          int64_t S, int64_t H, int64_t D, int64_t row_stride, float softmax_scale,
+                          int two_term, void* workspace, size_t workspace_bytes, void* stream);
 /* Synchronises `stream` and reports KB200_ERR_TIMEOUT if a bounded device-side
  * wait of the last attention launch on `workspace` gave up (the kernel then
  * skipped its remaining work instead of hanging). */

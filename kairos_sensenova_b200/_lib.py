@@ -50,7 +50,7 @@ class GdnPrologueArgs(ctypes.Structure):
     ]
 
 
-_ATTN_SIG = (ctypes.c_int, [ctypes.c_void_p] * 4 + [ctypes.c_int64] * 4 +
+_ATTN_SIG = (ctypes.c_int, [ctypes.c_void_p] * 4 + [ctypes.c_int64] * 5 +
              [ctypes.c_float, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p])
 
 # name -> (restype, argtypes); every symbol include/kb200.h declares

@@ -41,15 +41,21 @@ def attention_fp8(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, num_heads: 
         softmax_scale = D ** -0.5
     dev = q.device
     with torch.cuda.device(dev):
-        qc, kc, vc = (x.to(torch.bfloat16).contiguous() for x in (q, k, v))
-        o = torch.empty_like(qc)
+        qc, kc, vc = (x.to(torch.bfloat16) for x in (q, k, v))
+        ld = qc.stride(1)
+        # strided row views (e.g. column slices of one projection) are read in place
+        if not all(t.stride(2) == 1 and t.stride(1) == ld and (B == 1 or t.stride(0) == S * ld)
+                   and t.data_ptr() % 16 == 0 for t in (qc, kc, vc)) or ld % 8:
+            qc, kc, vc = (t.contiguous() for t in (qc, kc, vc))
+            ld = HD
+        o = torch.empty(B, S, HD, device=dev, dtype=torch.bfloat16)
         L = _lib.lib()
         nbytes = L.kb200_attn_fp8_workspace_size(B, S, num_heads, D, int(two_term))
         if nbytes == 0:
             raise ValueError(f'attention_fp8: unsupported shape B={B} S={S} H={num_heads} D={D} (D must be 128)')
         ws = torch.empty(nbytes, device=dev, dtype=torch.uint8)
         stream = torch.cuda.current_stream(dev).cuda_stream
-        args = (qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), o.data_ptr(), B, S, num_heads, D,
+        args = (qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), o.data_ptr(), B, S, num_heads, D, ld,
                 float(softmax_scale), int(two_term), ws.data_ptr(), nbytes, stream)
         if events is None:
             _lib.check(L.kb200_attn_fp8_fwd(*args), 'attention_fp8')

@@ -19,6 +19,7 @@ struct Params {
   uint8_t* vt8r; // [B, H, D, S_pad]  e4m3 residual of v             (two_term only)
   float* amax;   // [3, B, H]
   int B, S, H, S_pad;
+  int64_t ld;    // elements between consecutive tokens of q/k/v (H*D when contiguous)
   float softmax_scale;
   int vperm;     // 1: permute tokens inside 16-groups of vt8 for the mma.sync fragment order
   int two_term;  // 1: q and v carry a second e4m3 term (residual, same scale)

@@ -44,7 +44,7 @@ __global__ void __launch_bounds__(256) attn_amax_kernel(Params p) {
       const int t = t0 + (valid ? idx / vecs_per_tok : 0), c = valid ? (idx % vecs_per_tok) * 8 : 0;
       float m = 0.f;
       if (valid) {
-        uint4 raw = *reinterpret_cast<const uint4*>(x + ((size_t)b * p.S + t) * HD + c);
+        uint4 raw = *reinterpret_cast<const uint4*>(x + ((size_t)b * p.S + t) * p.ld + c);
         const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
 #pragma unroll
         for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(__bfloat162float(e[j])));
@@ -88,7 +88,7 @@ __global__ void __launch_bounds__(256) attn_quant_kernel(Params p) {
     const int r = idx / VPT, c = (idx % VPT) * 8, t = t0 + r;
     uint4 rq4 = make_uint4(0, 0, 0, 0), rk4 = rq4, rv4 = rq4;
     if (t < p.S) {
-      const size_t off = ((size_t)b * p.S + t) * H * D + h * D + c;
+      const size_t off = ((size_t)b * p.S + t) * p.ld + h * D + c;
       rq4 = *reinterpret_cast<const uint4*>(p.q + off);
       rk4 = *reinterpret_cast<const uint4*>(p.k + off);
       rv4 = *reinterpret_cast<const uint4*>(p.v + off);
@@ -392,9 +392,12 @@ bool use_tc() {
 }
 
 int attn_setup(attn::Params& p, AttnWs& w, const void* q, const void* k, const void* v, void* o,
-               int64_t B, int64_t S, int64_t H, int64_t D, float softmax_scale, int two_term,
-               void* workspace, size_t workspace_bytes) {
+               int64_t B, int64_t S, int64_t H, int64_t D, int64_t row_stride, float softmax_scale,
+               int two_term, void* workspace, size_t workspace_bytes) {
   if (int e = attn_validate(q, k, v, o, B, S, H, D)) return e;
+  if (row_stride == 0) row_stride = H * D;
+  if (row_stride < H * D || row_stride % 8)
+    return set_error(KB200_ERR_ALIGN, "attn_fp8: row_stride must be >= H*D and a multiple of 8");
   w = attn_ws(B, S, H, two_term);
   if (!workspace || workspace_bytes < w.total)
     return set_error(KB200_ERR_WORKSPACE, "attn_fp8: workspace needs %zu bytes, got %zu", w.total,
@@ -417,6 +420,7 @@ int attn_setup(attn::Params& p, AttnWs& w, const void* q, const void* k, const v
   p.S = (int)S;
   p.H = (int)H;
   p.S_pad = w.S_pad;
+  p.ld = row_stride;
   p.softmax_scale = softmax_scale;
   p.vperm = use_tc() ? 0 : 1;
   p.two_term = two_term ? 1 : 0;
@@ -445,12 +449,12 @@ int attn_attend(const attn::Params& p, const AttnWs& w, cudaStream_t st) {
 
 #define KB_ATTN_ARGS                                                                         \
   const void *q, const void *k, const void *v, void *o, int64_t B, int64_t S, int64_t H,    \
-      int64_t D, float softmax_scale, int two_term, void *workspace, size_t workspace_bytes, \
-      void *stream
+      int64_t D, int64_t row_stride, float softmax_scale, int two_term, void *workspace,           \
+      size_t workspace_bytes, void *stream
 #define KB_ATTN_SETUP                                                                          \
   attn::Params p;                                                                              \
   AttnWs w;                                                                                    \
-  if (int e = attn_setup(p, w, q, k, v, o, B, S, H, D, softmax_scale, two_term, workspace,     \
+  if (int e = attn_setup(p, w, q, k, v, o, B, S, H, D, row_stride, softmax_scale, two_term, workspace, \
                          workspace_bytes))                                                     \
     return e;                                                                                  \
   cudaStream_t st = static_cast<cudaStream_t>(stream);

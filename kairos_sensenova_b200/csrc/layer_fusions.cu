@@ -38,52 +38,78 @@ struct PrologueParams {
   int allow_neg_eigval;
 };
 
-// Grid (ceil(T / 32), ceil(maxC / 256), B * 4): z = 4*b + {0,1,2: conv q,k,v; 3: gates}.
-// Conv: each thread owns 8 consecutive channels of one token (16-byte vectors);
-// the W-1 previous tokens come from L1/L2 (each input row is read W times).
-__global__ void __launch_bounds__(256) gdn_prologue_kernel(PrologueParams p) {
+constexpr int PRO_RUN = 64;   // tokens per thread run (sliding window)
+
+// Grid (ceil(T / PRO_RUN), ceil(maxC / 1024), B * 4): z = 4*b + {0,1,2: conv q,k,v; 3: gates}.
+// Conv: each thread owns 8 consecutive channels and slides down a run of
+// PRO_RUN tokens keeping the last W input rows in registers, so every input
+// row is read once (plus W-1 halo rows per run) and the weights once per run.
+__global__ void __launch_bounds__(128) gdn_prologue_kernel(PrologueParams p) {
   const int which = blockIdx.z & 3, bb = blockIdx.z >> 2;
-  const int tok0 = blockIdx.x * 32;
+  const int tok0 = blockIdx.y * PRO_RUN;
+  const int tend = min(p.T, tok0 + PRO_RUN);
   if (which < 3) {
     const ConvSet cs = p.set[which];
-    const int c8 = (blockIdx.y * 32 + (threadIdx.x & 31)) * 8;
+    const int c8 = (blockIdx.x * 128 + threadIdx.x) * 8;
     if (c8 >= cs.C) return;
+    // weights right-aligned into 4 taps: tap i multiplies x[t - 3 + i] (leading taps zero when W < 4)
     float w[8][4];
 #pragma unroll
     for (int j = 0; j < 8; ++j)
 #pragma unroll
-      for (int i = 0; i < 4; ++i) w[j][i] = (i < p.W) ? cs.w[(c8 + j) * p.W + i] : 0.f;
+      for (int i = 0; i < 4; ++i) {
+        const int wi = i - (4 - p.W);
+        w[j][i] = (wi >= 0) ? cs.w[(c8 + j) * p.W + wi] : 0.f;
+      }
     float bias[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) bias[j] = cs.bias ? cs.bias[c8 + j] : 0.f;
-    for (int tt = threadIdx.x >> 5; tt < 32; tt += 8) {
-      const int t = tok0 + tt;
-      if (t >= p.T) break;
-      float acc[8];
+    const __nv_bfloat16* xb = cs.x + (size_t)bb * p.T * cs.ldx + c8;
+    // window: win[3] = x[t], win[2] = x[t-1], ...; rows before the sequence start are zero
+    float win[4][8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) acc[j] = bias[j];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        if (i >= p.W) break;
-        const int ts = t - (p.W - 1) + i;
-        if (ts < 0) continue;
-        uint4 raw = *reinterpret_cast<const uint4*>(cs.x + ((size_t)bb * p.T + ts) * cs.ldx + c8);
+    for (int i = 0; i < 3; ++i) {
+      const int ts = tok0 - 3 + i;
+      if (ts >= 0) {
+        uint4 raw = *reinterpret_cast<const uint4*>(xb + (size_t)ts * cs.ldx);
         const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[j] += __bfloat162float(e[j]) * w[j][i];
+        for (int j = 0; j < 8; ++j) win[i][j] = __bfloat162float(e[j]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) win[i][j] = 0.f;
+      }
+    }
+    for (int t = tok0; t < tend; ++t) {
+      {
+        uint4 raw = *reinterpret_cast<const uint4*>(xb + (size_t)t * cs.ldx);
+        const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) win[3][j] = __bfloat162float(e[j]);
       }
       uint4 outv;
       uint32_t* ov = reinterpret_cast<uint32_t*>(&outv);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float y0 = acc[2 * j], y1 = acc[2 * j + 1];
-        ov[j] = pack_bf16(y0 / (1.f + __expf(-y0)), y1 / (1.f + __expf(-y1)));
+      for (int j = 0; j < 8; j += 2) {
+        float y[2];
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          float acc = bias[j + q];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc = fmaf(win[i][j + q], w[j + q][i], acc);
+          y[q] = acc / (1.f + __expf(-acc));
+        }
+        ov[j / 2] = pack_bf16(y[0], y[1]);
       }
       *reinterpret_cast<uint4*>(cs.y + ((size_t)bb * p.T + t) * cs.ldy + c8) = outv;
+#pragma unroll
+      for (int i = 0; i < 3; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) win[i][j] = win[i + 1][j];
     }
   } else {
-    if (blockIdx.y != 0) return;
-    for (int idx = threadIdx.x; idx < 32 * p.H; idx += blockDim.x) {
+    if (blockIdx.x != 0) return;
+    for (int idx = threadIdx.x; idx < PRO_RUN * p.H; idx += blockDim.x) {
       const int t = tok0 + idx / p.H, h = idx % p.H;
       if (t >= p.T) break;
       const size_t row = (size_t)bb * p.T + t;
@@ -191,8 +217,9 @@ extern "C" int kb200_gdn_prologue(const KB200GdnPrologueArgs* a, void* stream) {
   p.H = (int)a->H;
   p.W = a->W;
   p.allow_neg_eigval = a->allow_neg_eigval;
-  dim3 grid((unsigned)((a->T + 31) / 32), (unsigned)((maxc / 8 + 31) / 32), (unsigned)(a->B * 4));
-  fuse::gdn_prologue_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  dim3 grid((unsigned)((maxc / 8 + 127) / 128), (unsigned)((a->T + fuse::PRO_RUN - 1) / fuse::PRO_RUN),
+            (unsigned)(a->B * 4));
+  fuse::gdn_prologue_kernel<<<grid, 128, 0, static_cast<cudaStream_t>(stream)>>>(p);
   return check_launch("gdn_prologue_kernel");
 }
 

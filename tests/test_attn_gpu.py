@@ -81,3 +81,15 @@ def test_attn_module_errors():
         AttentionModule(2)(x, x, x, attn_mask=torch.ones(8, 8, device='cuda'))
     with pytest.raises(ValueError):
         AttentionModule(4)(x, x, x)     # D = 64 unsupported
+
+
+def test_attn_fp8_strided_qkv_views_match_contiguous():
+    """q/k/v as column slices of one fused projection are read in place."""
+    from kairos_sensenova_b200.attention import attention_fp8
+    gen = torch.Generator().manual_seed(31)
+    S, H = 700, 2
+    fused = torch.randn(1, S, 3 * H * 128 + 8, generator=gen).bfloat16().cuda()
+    q, k, v = (fused[..., i * H * 128:(i + 1) * H * 128] for i in range(3))
+    o1 = attention_fp8(q, k, v, H)
+    o2 = attention_fp8(q.contiguous(), k.contiguous(), v.contiguous(), H)
+    assert torch.equal(o1, o2)
