@@ -88,6 +88,22 @@ size_t kb200_gdn_noalloc_scratch_bytes(void);
 int kb200_gdn_chunk_fwd_noalloc(const KB200GdnArgs* a, void* stream);
 
 /* ---------------------------------------------------------------------
+ * Attention prologue: y = RoPE(bf16(RMSNorm(x) * weight)) for each token row.
+ * Replaces SelfAttention.forward's q/k path (kairos/modules/dits/kairos_dit.py:452-456):
+ * FusedRMSNorm over the full `dim` channels (eps, weight [dim] fp32 or NULL)
+ * then rope_apply (kairos_dit.py:324-329): per head of `head_dim` channels, pair
+ * (2j, 2j+1) -> complex product with (cos, sin) = cos_sin[row][j] ([rows,
+ * head_dim/2, 2] fp32).  Channel c of a row lives at
+ *   base + (h / heads_per_block) * block_stride + row * ld + (h % heads_per_block) * head_dim + c % head_dim,
+ * h = c / head_dim (heads_per_block = dim / head_dim for a plain [rows, ld] matrix),
+ * so q/k can be normalised in place inside a destination-grouped projection.
+ * x == y is allowed.
+ * --------------------------------------------------------------------- */
+int kb200_rmsnorm_rope(const void* x, void* y, int64_t rows, int64_t dim, int64_t head_dim, int64_t ld,
+                       int64_t heads_per_block, int64_t block_stride, const float* weight,
+                       const float* cos_sin, float eps, void* stream);
+
+/* ---------------------------------------------------------------------
  * Softmax attention with FP8-e4m3 Q/K/V, per-(batch, head) amax scaling
  * (scale = amax/448), fp32 softmax and accumulation, bf16 output.
  * Replaces the attention core called by AttentionModule.forward

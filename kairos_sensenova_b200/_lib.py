@@ -60,6 +60,8 @@ SIGNATURES = {
     'kb200_gdn_workspace_size': (ctypes.c_size_t, [ctypes.POINTER(GdnArgs)]),
     'kb200_gdn_chunk_fwd': (ctypes.c_int, [ctypes.POINTER(GdnArgs), ctypes.c_void_p,
                                            ctypes.c_size_t, ctypes.c_void_p]),
+    'kb200_rmsnorm_rope': (ctypes.c_int, [ctypes.c_void_p] * 2 + [ctypes.c_int64] * 6 +
+                           [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_float, ctypes.c_void_p]),
     'kb200_gdn_noalloc_scratch_bytes': (ctypes.c_size_t, []),
     'kb200_gdn_chunk_fwd_noalloc': (ctypes.c_int, [ctypes.POINTER(GdnArgs), ctypes.c_void_p]),
     'kb200_attn_fp8_workspace_size': (ctypes.c_size_t, [ctypes.c_int64] * 4 + [ctypes.c_int]),

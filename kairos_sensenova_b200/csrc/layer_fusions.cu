@@ -174,6 +174,49 @@ __global__ void __launch_bounds__(256) rmsnorm_gated_kernel(const __nv_bfloat16*
   }
 }
 
+// Attention prologue: y = RoPE(bf16(RMSNorm_dim(x) * w)) per token row, in place allowed.
+// RMSNorm over the full `dim` channels (apex FusedRMSNorm as used at
+// kairos_dit.py:437-438,453-454); RoPE per head on channel pairs (2j, 2j+1) as
+// the complex product with (cos, sin) of the token (rope_apply, kairos_dit.py:324-329).
+// Channel c of row t lives at base + (h / hpb) * bstride + t * ld + (h % hpb) * hd + c % hd,
+// h = c / hd, so q/k can be read straight out of a destination-grouped projection.
+// One CTA per row, one 8-channel vector per thread (blockDim = dim / 8).
+__global__ void rmsnorm_rope_kernel(const __nv_bfloat16* x, __nv_bfloat16* y, int dim, int hd, int64_t ld,
+                                    int hpb, int64_t bstride, const float* __restrict__ w,
+                                    const float* __restrict__ cs, float eps) {
+  __shared__ float red[32];
+  const int t = blockIdx.x, c = threadIdx.x * 8;
+  const int h = c / hd, cc = c % hd;
+  const int64_t off = (int64_t)(h / hpb) * bstride + (int64_t)t * ld + (int64_t)(h % hpb) * hd + cc;
+  uint4 raw = *reinterpret_cast<const uint4*>(x + off);
+  const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
+  float v[8];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) { v[j] = __bfloat162float(e[j]); ss += v[j] * v[j]; }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float a = threadIdx.x < (blockDim.x + 31) / 32 ? red[threadIdx.x] : 0.f;
+    a = warp_sum(a);
+    if (threadIdx.x == 0) red[0] = a;
+  }
+  __syncthreads();
+  const float rstd = 1.f / sqrtf(red[0] / dim + eps);
+  uint4 outv;
+  uint32_t* ov = reinterpret_cast<uint32_t*>(&outv);
+  const float* csr = cs + ((int64_t)t * (hd / 2) + cc / 2) * 2;
+#pragma unroll
+  for (int j = 0; j < 8; j += 2) {
+    const float a = bf16_round(v[j] * rstd * (w ? w[c + j] : 1.f));
+    const float b = bf16_round(v[j + 1] * rstd * (w ? w[c + j + 1] : 1.f));
+    const float co = csr[j], si = csr[j + 1];
+    ov[j / 2] = pack_bf16(a * co - b * si, a * si + b * co);
+  }
+  *reinterpret_cast<uint4*>(y + off) = outv;
+}
+
 }  // namespace fuse
 }  // namespace kb
 
@@ -244,4 +287,20 @@ extern "C" int kb200_rmsnorm_gated(const void* x, const void* gate, const float*
   else if (D == 256) fuse::rmsnorm_gated_kernel<8><<<grid, 256, 0, st>>>(xb, gb, weight, yb, rows, hh, ld_gate, eps);
   else fuse::rmsnorm_gated_kernel<16><<<grid, 256, 0, st>>>(xb, gb, weight, yb, rows, hh, ld_gate, eps);
   return check_launch("rmsnorm_gated_kernel");
+}
+
+extern "C" int kb200_rmsnorm_rope(const void* x, void* y, int64_t rows, int64_t dim, int64_t head_dim,
+                                  int64_t ld, int64_t heads_per_block, int64_t block_stride,
+                                  const float* weight, const float* cos_sin, float eps, void* stream) {
+  if (!x || !y || !cos_sin) return set_error(KB200_ERR_INVALID, "rmsnorm_rope: null pointer");
+  if (rows < 0 || dim <= 0 || dim % 8 || dim / 8 > 1024 || head_dim <= 0 || head_dim % 8 ||
+      dim % head_dim || heads_per_block <= 0)
+    return set_error(KB200_ERR_INVALID, "rmsnorm_rope: need dim %% 8 == 0, dim <= 8192, head_dim | dim");
+  if (ld % 8 || block_stride % 8 || !aligned16(x) || !aligned16(y))
+    return set_error(KB200_ERR_ALIGN, "rmsnorm_rope: rows must be 16-byte aligned");
+  if (rows == 0) return KB200_OK;
+  fuse::rmsnorm_rope_kernel<<<(unsigned)rows, (unsigned)(dim / 8), 0, static_cast<cudaStream_t>(stream)>>>(
+      (const __nv_bfloat16*)x, (__nv_bfloat16*)y, (int)dim, (int)head_dim, ld, (int)heads_per_block,
+      block_stride, weight, cos_sin, eps);
+  return check_launch("rmsnorm_rope_kernel");
 }

@@ -85,3 +85,59 @@ def rms_norm_gated(x: torch.Tensor, gate: torch.Tensor, weight: torch.Tensor, ep
                                                    rows, H, D, g2.stride(0), float(eps), _stream(dev)),
                    'rms_norm_gated')
     return y
+
+
+def freqs_cis_3d(head_dim: int, f: int, h: int, w: int, theta: float = 10000.0) -> torch.Tensor:
+    """Per-token complex RoPE factors [f*h*w, head_dim/2] for a (frame, height,
+    width) latent grid: the frame axis gets head_dim - 2*(head_dim//3) channels,
+    height and width head_dim//3 each (``precompute_freqs_cis_3d``,
+    ``kairos_dit.py:312-315``; per-token layout as ``KairosDiT.forward``,
+    ``kairos_dit.py:1217-1221``)."""
+    def one(dim, end):
+        fr = 1.0 / (theta ** (torch.arange(0, dim, 2)[: dim // 2].double() / dim))
+        return torch.polar(torch.ones(end, dim // 2, dtype=torch.float64),
+                           torch.outer(torch.arange(end, dtype=torch.float64), fr))
+    ff = one(head_dim - 2 * (head_dim // 3), f)
+    fh = one(head_dim // 3, h)
+    fw = one(head_dim // 3, w)
+    return torch.cat([ff.view(f, 1, 1, -1).expand(f, h, w, -1), fh.view(1, h, 1, -1).expand(f, h, w, -1),
+                      fw.view(1, 1, w, -1).expand(f, h, w, -1)], dim=-1).reshape(f * h * w, -1)
+
+
+def rope_table(freqs: torch.Tensor, device) -> torch.Tensor:
+    """Complex factors [S, D/2] (or [S, 1, D/2]) -> interleaved (cos, sin) fp32 [S, D/2, 2]."""
+    fr = freqs.reshape(freqs.shape[0], -1)
+    return torch.stack([fr.real, fr.imag], dim=-1).to(device=device, dtype=torch.float32).contiguous()
+
+
+def rmsnorm_rope(x: torch.Tensor, weight, cos_sin: torch.Tensor, head_dim: int, eps: float = 1e-6,
+                 out: torch.Tensor | None = None, rows: int | None = None, dim: int | None = None,
+                 ld: int | None = None, heads_per_block: int | None = None, block_stride: int = 0):
+    """``RoPE(RMSNorm(x) * weight)`` per token row (``SelfAttention.forward``,
+    ``kairos_dit.py:452-456``).  ``x``: [..., dim] bf16 (rows = all leading
+    elements) or, with ``rows/dim/ld/heads_per_block/block_stride``, a
+    destination-grouped projection view; ``out`` defaults to a new tensor
+    (pass ``out=x`` to work in place)."""
+    dev = x.device
+    if dev.type != 'cuda':
+        raise RuntimeError('rmsnorm_rope: CUDA tensors required (no CPU path)')
+    if dim is None:
+        xc = x.to(torch.bfloat16).contiguous()
+        dim = xc.shape[-1]
+        rows = xc.numel() // dim
+        ld = dim
+        heads_per_block = dim // head_dim
+        x = xc
+    if out is None:
+        out = torch.empty_like(x)
+    w = None if weight is None else weight.to(dev, torch.float32).contiguous()
+    cs = cos_sin.to(dev, torch.float32).contiguous()
+    if cs.numel() < rows * head_dim:
+        raise ValueError('rmsnorm_rope: cos/sin table smaller than rows x head_dim/2 x 2')
+    with torch.cuda.device(dev):
+        _lib.check(_lib.lib().kb200_rmsnorm_rope(x.data_ptr(), out.data_ptr(), rows, dim, head_dim, ld,
+                                                  heads_per_block, block_stride,
+                                                  None if w is None else w.data_ptr(), cs.data_ptr(),
+                                                  float(eps), _stream(dev)),
+                   'rmsnorm_rope')
+    return out

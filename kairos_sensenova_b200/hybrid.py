@@ -19,7 +19,8 @@ re-partitioned Ulysses-style instead of the reference's per-owner broadcast):
 Attention chain (``SelfAttentionTP.forward``, ``kairos_dit.py:603-650``):
   q|k|v projection grouped by destination, seq->head all-to-all, FP8
   attention on the rank's heads, head->seq all-to-all, ``o`` projection.
-  The q/k RMSNorm and RoPE of the reference layer are not part of this chain.
+  q and k get the layer's full-dimension RMSNorm and 3-D RoPE in place in the
+  projection buffer before the exchange (one fused kernel, ``kairos_dit.py:452-456``).
 """
 from __future__ import annotations
 
@@ -29,7 +30,7 @@ import torch
 import torch.distributed as dist
 
 from .attention import attention_fp8
-from .fused_ops import gdn_prologue, rms_norm_gated
+from .fused_ops import freqs_cis_3d, gdn_prologue, rms_norm_gated, rmsnorm_rope, rope_table
 from .gated_delta_rule import chunk_gated_delta_rule
 
 
@@ -39,7 +40,8 @@ def _round8(n):
 
 class HybridBlock:
     def __init__(self, hidden=3072, heads=24, head_dim=128, world=1, rank=0, group=None,
-                 device='cuda', seed=3, conv_size=4, norm_eps=1e-5, two_term=True):
+                 device='cuda', seed=3, conv_size=4, norm_eps=1e-5, two_term=True, grid=(21, 30, 52),
+                 attn_eps=1e-6):
         assert heads % world == 0, 'heads must divide evenly over ranks'
         self.hidden, self.H, self.D = hidden, heads, head_dim
         self.P, self.rank, self.group = world, rank, group
@@ -66,6 +68,10 @@ class HybridBlock:
                        + math.log(0.001)).clamp(min=1e-4)
         self.dt_bias = (dt + torch.log(-torch.expm1(-dt))).float()
         self.o_norm_w = torch.ones(head_dim, device=device)
+        # attention q/k RMSNorm weights (FusedRMSNorm init: ones) and the 3-D RoPE grid
+        self.nq = torch.ones(HD, device=device)
+        self.nk = torch.ones(HD, device=device)
+        self.grid, self.attn_eps, self._rope = grid, attn_eps, None
         self._pack()
 
     # ------------------------------------------------------------------ layout
@@ -125,11 +131,25 @@ class HybridBlock:
         y = rms_norm_gated(o_seq.reshape(Tl, self.H, D), gate.reshape(Tl, self.H, D), self.o_norm_w, self.eps)
         return y.reshape(Tl, -1) @ self.WoT
 
+    def rope(self, T):
+        """(cos, sin) table [T, D/2, 2] of the 3-D RoPE grid (a 1-D frame axis when
+        the grid does not hold T tokens)."""
+        if self._rope is None or self._rope.shape[0] != T:
+            f, h, w = self.grid if self.grid[0] * self.grid[1] * self.grid[2] == T else (T, 1, 1)
+            self._rope = rope_table(freqs_cis_3d(self.D, f, h, w), self.W_attn.device)
+        return self._rope
+
     def attn_chain(self, x_local, events=None):
         Tl = x_local.shape[0]
         T = Tl * self.P
         Hl, D = self.Hl, self.D
         send = torch.matmul(x_local.unsqueeze(0), self.W_attn)          # [P, Tl, 3*Hl*D]
+        # q/k RMSNorm over all heads + RoPE, in place, sequence-sharded (before the exchange)
+        cs = self.rope(T)[self.rank * Tl:(self.rank + 1) * Tl]
+        for col, wgt in ((0, self.nq), (Hl * D, self.nk)):
+            view = send[..., col:]
+            rmsnorm_rope(view, wgt, cs, D, eps=self.attn_eps, out=view, rows=Tl, dim=self.H * D,
+                         ld=self.C_attn, heads_per_block=Hl, block_stride=Tl * self.C_attn)
         recv = self._a2a(send).reshape(T, self.C_attn)
         q, k, v = (recv[:, i * Hl * D:(i + 1) * Hl * D].reshape(1, T, Hl * D) for i in range(3))
         o = attention_fp8(q, k, v, Hl, two_term=self.two_term, events=events)
@@ -143,5 +163,5 @@ class HybridBlock:
         return self.attn_chain(y, events)
 
     # kernel launches of this library per forward(): prologue, 3 GDN kernels,
-    # gated RMSNorm; amax, quantise, attention
-    LAUNCHES_PER_STEP = 8
+    # gated RMSNorm; q and k RMSNorm+RoPE, amax, quantise, attention
+    LAUNCHES_PER_STEP = 10

@@ -12,7 +12,7 @@ import torch
 
 from .attention import sdpa_reference
 from .gdn import gdn_chunk
-from .layers import gates, rmsnorm_gated, short_conv_silu
+from .layers import gates, rmsnorm_gated, rmsnorm_rope, short_conv_silu
 
 
 def gdn_chain(w, x, H, D, eps=1e-5, heads=None):
@@ -34,11 +34,37 @@ def gdn_chain(w, x, H, D, eps=1e-5, heads=None):
     return y @ w['Wo'][:, cols].t()
 
 
-def attn_chain(w, x, H, D, heads=None):
+def freqs_cis_3d(D, f, h, w, theta=10000.0):
+    """Per-token complex RoPE factors (``kairos_dit.py:312-322,1217-1221``)."""
+    def one(dim, end):
+        fr = 1.0 / (theta ** (torch.arange(0, dim, 2)[: dim // 2].double() / dim))
+        ang = torch.outer(torch.arange(end, dtype=torch.float64), fr)
+        return torch.polar(torch.ones_like(ang), ang)
+    a, b, c = one(D - 2 * (D // 3), f), one(D // 3, h), one(D // 3, w)
+    return torch.cat([a.view(f, 1, 1, -1).expand(f, h, w, -1), b.view(1, h, 1, -1).expand(f, h, w, -1),
+                      c.view(1, 1, w, -1).expand(f, h, w, -1)], -1).reshape(f * h * w, -1)
+
+
+def attn_chain(w, x, H, D, heads=None, freqs=None, eps=1e-6, work_share=False):
+    """q/k projections with full-dim RMSNorm + RoPE (``SelfAttention.forward``,
+    ``kairos_dit.py:452-456``), SDPA, output projection.  With ``heads`` only
+    those heads' attention is computed and the norm still spans all heads;
+    ``work_share=True`` (CPU timing samples only) projects just those heads and
+    normalises over their channels, so the sample does exactly their share of
+    the work."""
     T = x.shape[0]
     hs = list(range(H)) if heads is None else list(heads)
     cols = torch.cat([torch.arange(h * D, (h + 1) * D) for h in hs])
-    q, k, v = ((x @ w[n][cols].t())[None] for n in ('Aq', 'Ak', 'Av'))
+    if freqs is None:
+        freqs = freqs_cis_3d(D, T, 1, 1)
+    nq, nk = w.get('nq', torch.ones(H * D)), w.get('nk', torch.ones(H * D))
+    if work_share:
+        q = rmsnorm_rope((x @ w['Aq'][cols].t())[None], nq[cols], freqs, len(hs), eps).float()
+        k = rmsnorm_rope((x @ w['Ak'][cols].t())[None], nk[cols], freqs, len(hs), eps).float()
+    else:
+        q = rmsnorm_rope((x @ w['Aq'].t())[None], nq, freqs, H, eps).float()[..., cols]
+        k = rmsnorm_rope((x @ w['Ak'].t())[None], nk, freqs, H, eps).float()[..., cols]
+    v = (x @ w['Av'][cols].t())[None]
     o = sdpa_reference(q, k, v, len(hs))[0]
     return o @ w['Ao'][:, cols].t()
 
@@ -50,5 +76,5 @@ def hybrid_forward(w, x, H, D, eps=1e-5):
 def weights_of(block):
     """CPU fp32 copies of a kairos_sensenova_b200.hybrid.HybridBlock's weights."""
     names = ('Wq', 'Wk', 'Wv', 'Wg', 'Wa', 'Wb', 'Wo', 'Aq', 'Ak', 'Av', 'Ao', 'cq', 'ck', 'cv',
-             'A_log', 'dt_bias', 'o_norm_w')
+             'A_log', 'dt_bias', 'o_norm_w', 'nq', 'nk')
     return {n: getattr(block, n).detach().float().cpu() for n in names}

@@ -78,3 +78,16 @@ def head_to_seq_expected(full, rank, world):
     """full [B, N, D] -> rank's [B, N/P, D] after all2all_head_to_seq."""
     n = full.shape[1] // world
     return full[:, rank * n:(rank + 1) * n]
+
+
+def rmsnorm_rope(x, weight, freqs, num_heads, eps=1e-6):
+    """``rope_apply(norm(x))`` as the reference computes it: apex FusedRMSNorm
+    over the full dim in fp32 -> bf16, then (``kairos_dit.py:324-329``) fp16
+    complex pairs times the (double) complex factors, result cast to bf16.
+    x: [B, S, N*D]; freqs: complex [S, D/2]."""
+    xf = x.float()
+    y = (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * weight.float()).bfloat16()
+    B, S, HD = y.shape
+    c = torch.view_as_complex(y.reshape(B, S, num_heads, -1, 2).to(torch.float16).float().contiguous())
+    out = torch.view_as_real(c.to(torch.complex128) * freqs.reshape(1, S, 1, -1)).flatten(3)
+    return out.reshape(B, S, HD).bfloat16()

@@ -83,3 +83,32 @@ def test_gated_deltanet_layer_matches_oracle():
     ref = ol.gated_deltanet_forward({k: v.bfloat16().float() for k, v in sd.items()}, x.float(), H, hd, hd)
     assert o.shape == (1, 300, hidden)
     assert max_rel(o, ref) < 2e-2
+
+
+def test_rmsnorm_rope_matches_reference_math():
+    from kairos_sensenova_b200.fused_ops import freqs_cis_3d, rmsnorm_rope, rope_table
+    gen = torch.Generator().manual_seed(40)
+    H, D = 4, 128
+    fr = freqs_cis_3d(D, 3, 5, 7)                      # 105 tokens on a 3x5x7 grid
+    S = fr.shape[0]
+    x = (torch.randn(1, S, H * D, generator=gen) * 3).bfloat16()
+    w = torch.rand(H * D, generator=gen) + 0.5
+    y = rmsnorm_rope(x.cuda(), w.cuda(), rope_table(fr, 'cuda'), D)
+    ref = ol.rmsnorm_rope(x, w, fr, H)
+    assert max_rel(y, ref) < 1e-2
+
+
+def test_rmsnorm_rope_in_place_on_grouped_projection():
+    """q as the first column block of a destination-grouped [P, T, 3*Hl*D] buffer."""
+    from kairos_sensenova_b200.fused_ops import freqs_cis_3d, rmsnorm_rope, rope_table
+    gen = torch.Generator().manual_seed(41)
+    P, Hl, D, T = 2, 2, 128, 60
+    buf = torch.randn(P, T, 3 * Hl * D, generator=gen).bfloat16().cuda()
+    fr = freqs_cis_3d(D, 3, 4, 5)
+    cs = rope_table(fr, 'cuda')
+    q_full = torch.cat([buf[r, :, :Hl * D] for r in range(P)], dim=1)   # [T, P*Hl*D]
+    ref = rmsnorm_rope(q_full.unsqueeze(0).contiguous(), None, cs, D)[0]
+    rmsnorm_rope(buf, None, cs, D, out=buf, rows=T, dim=P * Hl * D, ld=3 * Hl * D, heads_per_block=Hl,
+                 block_stride=T * 3 * Hl * D)
+    got = torch.cat([buf[r, :, :Hl * D] for r in range(P)], dim=1)
+    assert torch.equal(got, ref)
