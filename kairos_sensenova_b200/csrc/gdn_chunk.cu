@@ -394,6 +394,7 @@ struct StateSmem {
   __nv_bfloat16 us[2][BT * LDV];
   __nv_bfloat16 hb[2][K * LDV];   // bf16 snapshot of the state (B operand of w h)
   __nv_bfloat16 vg[2][BT * LDV];  // gated v_new (B operand of k^T v)
+  __nv_bfloat16 vn[BT * LDV];     // v_new staged for coalesced 16-byte stores
   float gcs[2][BT];
 };
 
@@ -402,25 +403,43 @@ KB_DEVI void cp_async4(void* smem, const void* gmem, bool pred) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(smem_u32(smem)), "l"(gmem), "r"(n));
 }
 
+// Per-thread copy plan, fixed for the whole pass: thread tid copies 16-byte
+// vectors (row kr0 + i * KRS, column kc) of the w / k tiles, one vector (ur, uc)
+// of the u tile and, for tid < 64, the gate value of row tid.
 template <int K, int BV>
-KB_DEVI void state_issue_loads(StateSmem<K, BV>& sm, int buf, const Params& p, int t0, int L,
-                               int h, int v0, int V, int tid) {
-  const int H = p.H;
-  constexpr int KV = K / 8, VV = BV / 8;
-  for (int idx = tid; idx < BT * KV; idx += STATE_THREADS) {
-    const int r = idx / KV, cv = (idx % KV) * 8;
-    const bool ok = r < L;
-    const size_t off = ((size_t)(t0 + (ok ? r : 0)) * H + h) * K + cv;
-    cp_async16(&sm.ws[buf][r * StateSmem<K, BV>::LDK + cv], p.w + off, ok);
-    cp_async16(&sm.ks[buf][r * StateSmem<K, BV>::LDK + cv], p.kn + off, ok);
+struct StateCopyPlan {
+  static constexpr int VPR = K / 8, KRS = STATE_THREADS / VPR, KIT = BT / KRS;
+  int kr0, kc, ur, uc;
+  KB_DEVI StateCopyPlan(int tid) {
+    kr0 = tid / VPR;
+    kc = (tid % VPR) * 8;
+    ur = tid / (BV / 8);
+    uc = (tid % (BV / 8)) * 8;
   }
-  for (int idx = tid; idx < BT * VV; idx += STATE_THREADS) {
-    const int r = idx / VV, cv = (idx % VV) * 8;
+};
+
+template <int K, int BV>
+KB_DEVI void state_issue_loads(StateSmem<K, BV>& sm, int buf, const Params& p, const StateCopyPlan<K, BV>& cp,
+                               int t0, int L, int h, int v0, int V, int tid) {
+  using S = StateSmem<K, BV>;
+  using CP = StateCopyPlan<K, BV>;
+  const size_t HK = (size_t)p.H * K;
+  const __nv_bfloat16* wb = p.w + (size_t)t0 * HK + (size_t)h * K + cp.kc;
+  const __nv_bfloat16* kb = p.kn + (size_t)t0 * HK + (size_t)h * K + cp.kc;
+#pragma unroll
+  for (int i = 0; i < CP::KIT; ++i) {
+    const int r = cp.kr0 + i * CP::KRS;
     const bool ok = r < L;
-    const size_t off = ((size_t)(t0 + (ok ? r : 0)) * H + h) * V + v0 + cv;
-    cp_async16(&sm.us[buf][r * StateSmem<K, BV>::LDV + cv], p.u + off, ok);
+    const size_t off = (size_t)(ok ? r : 0) * HK;
+    cp_async16(&sm.ws[buf][r * S::LDK + cp.kc], wb + off, ok);
+    cp_async16(&sm.ks[buf][r * S::LDK + cp.kc], kb + off, ok);
   }
-  if (tid < BT) cp_async4(&sm.gcs[buf][tid], p.gc + (size_t)(t0 + (tid < L ? tid : 0)) * H + h, tid < L);
+  if (cp.ur < BT) {
+    const bool ok = cp.ur < L;
+    cp_async16(&sm.us[buf][cp.ur * S::LDV + cp.uc],
+               p.u + ((size_t)(t0 + (ok ? cp.ur : 0)) * p.H + h) * V + v0 + cp.uc, ok);
+  }
+  if (tid < BT) cp_async4(&sm.gcs[buf][tid], p.gc + (size_t)(t0 + (tid < L ? tid : 0)) * p.H + h, tid < L);
   cp_async_commit();
 }
 
@@ -460,7 +479,8 @@ __global__ void __launch_bounds__(STATE_THREADS) gdn_state_kernel(Params p) {
         const int cc = v0 + nn * 8 + 2 * t4 + (e & 1);
         hacc[m][nn][e] = p.h0 ? p.h0[((size_t)nh * K + r) * V + cc] : 0.f;
       }
-  if (NTn > 0) state_issue_loads<K, BV>(sm, 0, p, bos, min(BT, Tn), h, v0, V, tid);
+  const StateCopyPlan<K, BV> cplan(tid);
+  if (NTn > 0) state_issue_loads<K, BV>(sm, 0, p, cplan, bos, min(BT, Tn), h, v0, V, tid);
   const int rg = warp & 3, c0 = (warp >> 2) * (BV / 2);
 
   for (int it = 0; it < NTn; ++it) {
@@ -479,13 +499,17 @@ __global__ void __launch_bounds__(STATE_THREADS) gdn_state_kernel(Params p) {
         const uint32_t hi = pack_bf16(hacc[m][nn][2], hacc[m][nn][3]);
         *reinterpret_cast<uint32_t*>(&hb[r * S::LDV + cc]) = lo;
         *reinterpret_cast<uint32_t*>(&hb[(r + 8) * S::LDV + cc]) = hi;
-        *reinterpret_cast<uint32_t*>(hg + (size_t)r * V + v0 + cc) = lo;
-        *reinterpret_cast<uint32_t*>(hg + (size_t)(r + 8) * V + v0 + cc) = hi;
       }
     cp_async_wait<0>();
     __syncthreads();
+    // snapshot -> global h[chunk] as coalesced 16-byte vectors
+#pragma unroll
+    for (int i = 0; i < K * (BV / 8) / STATE_THREADS; ++i) {
+      const int idx = tid + i * STATE_THREADS, r = idx / (BV / 8), cv = (idx % (BV / 8)) * 8;
+      *reinterpret_cast<uint4*>(hg + (size_t)r * V + v0 + cv) = *reinterpret_cast<const uint4*>(&hb[r * S::LDV + cv]);
+    }
     if (it + 1 < NTn)
-      state_issue_loads<K, BV>(sm, buf ^ 1, p, t0 + BT, min(BT, Tn - (it + 1) * BT), h, v0, V, tid);
+      state_issue_loads<K, BV>(sm, buf ^ 1, p, cplan, t0 + BT, min(BT, Tn - (it + 1) * BT), h, v0, V, tid);
     // (b) v_new = u - w h   (rows 16 rg.., columns c0..c0+BV/2); two accumulator sets halve the chain
     const float glast = sm.gcs[buf][L - 1];
     __nv_bfloat16* vg = sm.vg[buf];
@@ -519,15 +543,17 @@ __global__ void __launch_bounds__(STATE_THREADS) gdn_state_kernel(Params p) {
         const float a1 = __high2float(u0) - (acc0[nn][1] + acc1[nn][1]);
         const float a2 = __low2float(u1) - (acc0[nn][2] + acc1[nn][2]);
         const float a3 = __high2float(u1) - (acc0[nn][3] + acc1[nn][3]);
-        if (r0 < L)
-          *reinterpret_cast<uint32_t*>(p.vnew + ((size_t)(t0 + r0) * H + h) * V + v0 + cc) = pack_bf16(a0, a1);
-        if (r1 < L)
-          *reinterpret_cast<uint32_t*>(p.vnew + ((size_t)(t0 + r1) * H + h) * V + v0 + cc) = pack_bf16(a2, a3);
+        *reinterpret_cast<uint32_t*>(&sm.vn[r0 * S::LDV + cc]) = pack_bf16(a0, a1);
+        *reinterpret_cast<uint32_t*>(&sm.vn[r1 * S::LDV + cc]) = pack_bf16(a2, a3);
         *reinterpret_cast<uint32_t*>(&vg[r0 * S::LDV + cc]) = pack_bf16(a0 * e0, a1 * e0);
         *reinterpret_cast<uint32_t*>(&vg[r1 * S::LDV + cc]) = pack_bf16(a2 * e1, a3 * e1);
       }
     }
     __syncthreads();
+    // v_new -> global as 16-byte vectors (rows < L)
+    if (cplan.ur < L)
+      *reinterpret_cast<uint4*>(p.vnew + ((size_t)(t0 + cplan.ur) * H + h) * V + v0 + cplan.uc) =
+          *reinterpret_cast<const uint4*>(&sm.vn[cplan.ur * S::LDV + cplan.uc]);
     // (c) h <- e^{g_last} h + k^T vg
     {
       const float dec = __expf(glast);
