@@ -236,6 +236,8 @@ def main():
         bf16_tf, hbm, kind = _peaks()
         fp8_peak = 2 * bf16_tf
         flops = 4.0 * T_FULL * T_FULL * HEAD_DIM * (HEADS // world)
+        units = T_FULL * (HEADS // world)
+        traffic = 42.0e6 * units / (8192 * 8) + 2.0 * units * HEAD_DIM
         achieved = flops / (attn_ms * 1e-3) / 1e12
         line = {
             'metric': METRIC, 'value': T_FULL / (step_ms * 1e-3) / 1e6, 'unit': 'Mtokens/s',
@@ -252,7 +254,9 @@ def main():
             'gpu_launches': blk.LAUNCHES_PER_STEP * args.steps,
             'roofline': {'kernel': 'attention (fp8)', 'bound': 'tensor', 'achieved': achieved,
                          'peak': fp8_peak, 'unit': 'TFLOP/s', 'frac': achieved / fp8_peak,
-                         'traffic': None, 'attn_ms': attn_ms,
+                         'traffic': traffic, 'attn_ms': attn_ms,
+                         'traffic_source': 'ncu dram read bytes of a B1 S8192 H8 capture (42.0 MB) scaled by '
+                                           'tokens x heads, plus the bf16 output bytes',
                          'peak_source': f'2x {kind} bf16 dense ({bf16_tf} TFLOP/s): FP8 dense rate'},
             'clocks': clocks,
         }
