@@ -68,21 +68,6 @@ KB_DEVI float ex2(float x) {
   return y;
 }
 
-// Packed fp32 pair arithmetic (Blackwell f32x2 instructions): one issue slot for two lanes.
-KB_DEVI float2 ffma2(float2 a, float2 b, float2 c) {
-  float2 d;
-  asm("{.reg .b64 ra, rb, rc, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n mov.b64 rc, {%6, %7};\n"
-      " fma.rn.f32x2 rd, ra, rb, rc;\n mov.b64 {%0, %1}, rd;}\n"
-      : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
-  return d;
-}
-KB_DEVI float2 fadd2(float2 a, float2 b) {
-  float2 d;
-  asm("{.reg .b64 ra, rb, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n"
-      " add.rn.f32x2 rd, ra, rb;\n mov.b64 {%0, %1}, rd;}\n"
-      : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-  return d;
-}
 
 KB_DEVI float fmax3(float a, float b, float c) {
   float d;

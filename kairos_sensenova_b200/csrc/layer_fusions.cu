@@ -38,78 +38,105 @@ struct PrologueParams {
   int allow_neg_eigval;
 };
 
-constexpr int PRO_RUN = 64;   // tokens per thread run (sliding window)
+constexpr int PT = 64, PC = 256, PTHREADS = 128;   // tokens and channels per CTA tile
+constexpr int PRUN = PT / (PTHREADS / (PC / 8));   // tokens per thread (16)
 
-// Grid (ceil(T / PRO_RUN), ceil(maxC / 1024), B * 4): z = 4*b + {0,1,2: conv q,k,v; 3: gates}.
-// Conv: each thread owns 8 consecutive channels and slides down a run of
-// PRO_RUN tokens keeping the last W input rows in registers, so every input
-// row is read once (plus W-1 halo rows per run) and the weights once per run.
-__global__ void __launch_bounds__(128) gdn_prologue_kernel(PrologueParams p) {
+// Two consecutive bf16 channels of a packed word as an fp32 pair.
+KB_DEVI float2 bf16x2_to_float2(uint32_t u) {
+  return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+}
+KB_DEVI float2 silu2(float2 a) {
+  const float2 e = fmul2(a, make_float2(-1.4426950408889634f, -1.4426950408889634f));   // -a log2(e)
+  float2 d;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(d.x) : "f"(e.x));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(d.y) : "f"(e.y));
+  d = fadd2(d, make_float2(1.f, 1.f));
+  float2 r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r.x) : "f"(d.x));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r.y) : "f"(d.y));
+  return fmul2(a, r);
+}
+
+// Grid (ceil(maxC / PC), ceil(T / PT), B * 4): z = 4*b + {0,1,2: conv q,k,v; 3: gates}.
+// Conv: the CTA stages its (PT + 3 halo) x PC input tile with cp.async in one
+// shot (every load in flight at once).  Each thread then owns 8 channels
+// (weights in registers as fp32 channel pairs) and slides a 4-row window down
+// PRUN consecutive tokens: one shared-memory row load and 16 packed FMAs per token.
+__global__ void __launch_bounds__(PTHREADS, 5) gdn_prologue_kernel(PrologueParams p) {
   const int which = blockIdx.z & 3, bb = blockIdx.z >> 2;
-  const int tok0 = blockIdx.y * PRO_RUN;
-  const int tend = min(p.T, tok0 + PRO_RUN);
+  const int tok0 = blockIdx.y * PT;
+  const int tid = threadIdx.x;
   if (which < 3) {
+    __shared__ __align__(16) __nv_bfloat16 tile[PT + 3][PC];
+    // channel c = 8 * grp + j lives at wsm[j][grp]: lanes (consecutive grp) read 16 B apart
+    __shared__ __align__(16) float wsm[8][PC / 8][4];
+    __shared__ float bsm[8][PC / 8];
     const ConvSet cs = p.set[which];
-    const int c8 = (blockIdx.x * 128 + threadIdx.x) * 8;
-    if (c8 >= cs.C) return;
-    // weights right-aligned into 4 taps: tap i multiplies x[t - 3 + i] (leading taps zero when W < 4)
-    float w[8][4];
-#pragma unroll
-    for (int j = 0; j < 8; ++j)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int wi = i - (4 - p.W);
-        w[j][i] = (wi >= 0) ? cs.w[(c8 + j) * p.W + wi] : 0.f;
-      }
-    float bias[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) bias[j] = cs.bias ? cs.bias[c8 + j] : 0.f;
-    const __nv_bfloat16* xb = cs.x + (size_t)bb * p.T * cs.ldx + c8;
-    // window: win[3] = x[t], win[2] = x[t-1], ...; rows before the sequence start are zero
-    float win[4][8];
-#pragma unroll
-    for (int i = 0; i < 3; ++i) {
-      const int ts = tok0 - 3 + i;
-      if (ts >= 0) {
-        uint4 raw = *reinterpret_cast<const uint4*>(xb + (size_t)ts * cs.ldx);
-        const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) win[i][j] = __bfloat162float(e[j]);
-      } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) win[i][j] = 0.f;
-      }
+    const int c0 = blockIdx.x * PC;
+    if (c0 >= cs.C) return;
+    const __nv_bfloat16* xb = cs.x + (size_t)bb * p.T * cs.ldx;
+    for (int idx = tid; idx < (PT + 3) * (PC / 8); idx += PTHREADS) {
+      const int r = idx / (PC / 8), cv = (idx % (PC / 8)) * 8;
+      const int t = tok0 - 3 + r;
+      const bool ok = t >= 0 && t < p.T && c0 + cv < cs.C;
+      cp_async16(&tile[r][cv], xb + (size_t)(ok ? t : 0) * cs.ldx + (ok ? c0 + cv : 0), ok);
     }
-    for (int t = tok0; t < tend; ++t) {
-      {
-        uint4 raw = *reinterpret_cast<const uint4*>(xb + (size_t)t * cs.ldx);
-        const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
+    cp_async_commit();
+    // weights right-aligned into 4 taps: tap i multiplies x[t - 3 + i] (leading taps zero when W < 4)
+    for (int idx = tid; idx < PC * 4; idx += PTHREADS) {
+      const int c = idx >> 2, wi = (idx & 3) - (4 - p.W);
+      wsm[c & 7][c >> 3][idx & 3] = (wi >= 0 && c0 + c < cs.C) ? cs.w[(size_t)(c0 + c) * p.W + wi] : 0.f;
+    }
+    for (int c = tid; c < PC; c += PTHREADS)
+      bsm[c & 7][c >> 3] = (cs.bias && c0 + c < cs.C) ? cs.bias[c0 + c] : 0.f;
+    const int grp = tid % (PC / 8), cv = grp * 8, tg = tid / (PC / 8);
+    const int c8 = c0 + cv;
+    cp_async_wait<0>();
+    __syncthreads();
+    if (c8 >= cs.C) return;
+    float2 wp[4][4], bp[4];   // [tap][channel pair]
 #pragma unroll
-        for (int j = 0; j < 8; ++j) win[3][j] = __bfloat162float(e[j]);
+    for (int q = 0; q < 4; ++q) {
+      const float4 w0 = *reinterpret_cast<const float4*>(wsm[2 * q][grp]);
+      const float4 w1 = *reinterpret_cast<const float4*>(wsm[2 * q + 1][grp]);
+      wp[0][q] = make_float2(w0.x, w1.x); wp[1][q] = make_float2(w0.y, w1.y);
+      wp[2][q] = make_float2(w0.z, w1.z); wp[3][q] = make_float2(w0.w, w1.w);
+      bp[q] = make_float2(bsm[2 * q][grp], bsm[2 * q + 1][grp]);
+    }
+    const int tl0 = tg * PRUN;
+    float2 win[4][4];   // ring of rows: row tl0 + r sits in slot r & 3
+#pragma unroll
+    for (int r = 0; r < 3; ++r) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(&tile[tl0 + r][cv]);
+      win[r][0] = bf16x2_to_float2(raw.x); win[r][1] = bf16x2_to_float2(raw.y);
+      win[r][2] = bf16x2_to_float2(raw.z); win[r][3] = bf16x2_to_float2(raw.w);
+    }
+    __nv_bfloat16* yrow = cs.y + ((size_t)bb * p.T + tok0 + tl0) * cs.ldy + c8;
+    const int nt = min(PRUN, p.T - tok0 - tl0);
+#pragma unroll
+    for (int k = 0; k < PRUN; ++k) {
+      if (k >= nt) break;
+      {
+        const uint4 raw = *reinterpret_cast<const uint4*>(&tile[tl0 + k + 3][cv]);
+        float2* w = win[(k + 3) & 3];
+        w[0] = bf16x2_to_float2(raw.x); w[1] = bf16x2_to_float2(raw.y);
+        w[2] = bf16x2_to_float2(raw.z); w[3] = bf16x2_to_float2(raw.w);
       }
       uint4 outv;
       uint32_t* ov = reinterpret_cast<uint32_t*>(&outv);
 #pragma unroll
-      for (int j = 0; j < 8; j += 2) {
-        float y[2];
+      for (int q = 0; q < 4; ++q) {
+        float2 a = bp[q];
 #pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          float acc = bias[j + q];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) acc = fmaf(win[i][j + q], w[j + q][i], acc);
-          y[q] = acc / (1.f + __expf(-acc));
-        }
-        ov[j / 2] = pack_bf16(y[0], y[1]);
+        for (int i = 0; i < 4; ++i) a = ffma2(win[(k + i) & 3][q], wp[i][q], a);
+        a = silu2(a);
+        ov[q] = pack_bf16(a.x, a.y);
       }
-      *reinterpret_cast<uint4*>(cs.y + ((size_t)bb * p.T + t) * cs.ldy + c8) = outv;
-#pragma unroll
-      for (int i = 0; i < 3; ++i)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) win[i][j] = win[i + 1][j];
+      *reinterpret_cast<uint4*>(yrow + (size_t)k * cs.ldy) = outv;
     }
   } else {
     if (blockIdx.x != 0) return;
-    for (int idx = threadIdx.x; idx < PRO_RUN * p.H; idx += blockDim.x) {
+    for (int idx = tid; idx < PT * p.H; idx += blockDim.x) {
       const int t = tok0 + idx / p.H, h = idx % p.H;
       if (t >= p.T) break;
       const size_t row = (size_t)bb * p.T + t;
@@ -180,41 +207,58 @@ __global__ void __launch_bounds__(256) rmsnorm_gated_kernel(const __nv_bfloat16*
 // the complex product with (cos, sin) of the token (rope_apply, kairos_dit.py:324-329).
 // Channel c of row t lives at base + (h / hpb) * bstride + t * ld + (h % hpb) * hd + c % hd,
 // h = c / hd, so q/k can be read straight out of a destination-grouped projection.
-// One CTA per row, one 8-channel vector per thread (blockDim = dim / 8).
-__global__ void rmsnorm_rope_kernel(const __nv_bfloat16* x, __nv_bfloat16* y, int dim, int hd, int64_t ld,
+// One CTA per RR rows (all loads issued up front), one 8-channel vector per
+// thread and row (blockDim = dim / 8).
+constexpr int RR = 4;
+__global__ void rmsnorm_rope_kernel(const __nv_bfloat16* x, __nv_bfloat16* y, int rows, int dim, int hd, int64_t ld,
                                     int hpb, int64_t bstride, const float* __restrict__ w,
                                     const float* __restrict__ cs, float eps) {
-  __shared__ float red[32];
-  const int t = blockIdx.x, c = threadIdx.x * 8;
+  __shared__ float red[RR][32];
+  const int c = threadIdx.x * 8;
   const int h = c / hd, cc = c % hd;
-  const int64_t off = (int64_t)(h / hpb) * bstride + (int64_t)t * ld + (int64_t)(h % hpb) * hd + cc;
-  uint4 raw = *reinterpret_cast<const uint4*>(x + off);
-  const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
-  float v[8];
-  float ss = 0.f;
+  const int64_t coff = (int64_t)(h / hpb) * bstride + (int64_t)(h % hpb) * hd + cc;
+  const int nw = (blockDim.x + 31) / 32;
+  uint4 raw[RR];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) { v[j] = __bfloat162float(e[j]); ss += v[j] * v[j]; }
-  ss = warp_sum(ss);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-  __syncthreads();
-  if (threadIdx.x < 32) {
-    float a = threadIdx.x < (blockDim.x + 31) / 32 ? red[threadIdx.x] : 0.f;
-    a = warp_sum(a);
-    if (threadIdx.x == 0) red[0] = a;
+  for (int q = 0; q < RR; ++q) {
+    const int t = blockIdx.x * RR + q;
+    raw[q] = t < rows ? *reinterpret_cast<const uint4*>(x + coff + (int64_t)t * ld) : make_uint4(0, 0, 0, 0);
+  }
+  float ss[RR];
+#pragma unroll
+  for (int q = 0; q < RR; ++q) {
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw[q]);
+    float a = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) { const float v = __bfloat162float(e[j]); a += v * v; }
+    ss[q] = warp_sum(a);
+    if ((threadIdx.x & 31) == 0) red[q][threadIdx.x >> 5] = ss[q];
   }
   __syncthreads();
-  const float rstd = 1.f / sqrtf(red[0] / dim + eps);
-  uint4 outv;
-  uint32_t* ov = reinterpret_cast<uint32_t*>(&outv);
-  const float* csr = cs + ((int64_t)t * (hd / 2) + cc / 2) * 2;
+  float wv[8];
 #pragma unroll
-  for (int j = 0; j < 8; j += 2) {
-    const float a = bf16_round(v[j] * rstd * (w ? w[c + j] : 1.f));
-    const float b = bf16_round(v[j + 1] * rstd * (w ? w[c + j + 1] : 1.f));
-    const float co = csr[j], si = csr[j + 1];
-    ov[j / 2] = pack_bf16(a * co - b * si, a * si + b * co);
+  for (int j = 0; j < 8; ++j) wv[j] = w ? w[c + j] : 1.f;
+#pragma unroll
+  for (int q = 0; q < RR; ++q) {
+    const int t = blockIdx.x * RR + q;
+    float tot = 0.f;
+    for (int i = 0; i < nw; ++i) tot += red[q][i];
+    if (t >= rows) continue;
+    const float rstd = 1.f / sqrtf(tot / dim + eps);
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw[q]);
+    const float* csr = cs + ((int64_t)t * (hd / 2) + cc / 2) * 2;
+    const float4 cs0 = *reinterpret_cast<const float4*>(csr), cs1 = *reinterpret_cast<const float4*>(csr + 4);
+    const float co[4] = {cs0.x, cs0.z, cs1.x, cs1.z}, si[4] = {cs0.y, cs0.w, cs1.y, cs1.w};
+    uint4 outv;
+    uint32_t* ov = reinterpret_cast<uint32_t*>(&outv);
+#pragma unroll
+    for (int j = 0; j < 8; j += 2) {
+      const float a = bf16_round(__bfloat162float(e[j]) * rstd * wv[j]);
+      const float bb = bf16_round(__bfloat162float(e[j + 1]) * rstd * wv[j + 1]);
+      ov[j / 2] = pack_bf16(a * co[j / 2] - bb * si[j / 2], a * si[j / 2] + bb * co[j / 2]);
+    }
+    *reinterpret_cast<uint4*>(y + coff + (int64_t)t * ld) = outv;
   }
-  *reinterpret_cast<uint4*>(y + off) = outv;
 }
 
 }  // namespace fuse
@@ -260,9 +304,9 @@ extern "C" int kb200_gdn_prologue(const KB200GdnPrologueArgs* a, void* stream) {
   p.H = (int)a->H;
   p.W = a->W;
   p.allow_neg_eigval = a->allow_neg_eigval;
-  dim3 grid((unsigned)((maxc / 8 + 127) / 128), (unsigned)((a->T + fuse::PRO_RUN - 1) / fuse::PRO_RUN),
+  dim3 grid((unsigned)((maxc + fuse::PC - 1) / fuse::PC), (unsigned)((a->T + fuse::PT - 1) / fuse::PT),
             (unsigned)(a->B * 4));
-  fuse::gdn_prologue_kernel<<<grid, 128, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  fuse::gdn_prologue_kernel<<<grid, fuse::PTHREADS, 0, static_cast<cudaStream_t>(stream)>>>(p);
   return check_launch("gdn_prologue_kernel");
 }
 
@@ -299,8 +343,9 @@ extern "C" int kb200_rmsnorm_rope(const void* x, void* y, int64_t rows, int64_t 
   if (ld % 8 || block_stride % 8 || !aligned16(x) || !aligned16(y))
     return set_error(KB200_ERR_ALIGN, "rmsnorm_rope: rows must be 16-byte aligned");
   if (rows == 0) return KB200_OK;
-  fuse::rmsnorm_rope_kernel<<<(unsigned)rows, (unsigned)(dim / 8), 0, static_cast<cudaStream_t>(stream)>>>(
-      (const __nv_bfloat16*)x, (__nv_bfloat16*)y, (int)dim, (int)head_dim, ld, (int)heads_per_block,
+  fuse::rmsnorm_rope_kernel<<<(unsigned)((rows + fuse::RR - 1) / fuse::RR), (unsigned)(dim / 8), 0,
+                               static_cast<cudaStream_t>(stream)>>>(
+      (const __nv_bfloat16*)x, (__nv_bfloat16*)y, (int)rows, (int)dim, (int)head_dim, ld, (int)heads_per_block,
       block_stride, weight, cos_sin, eps);
   return check_launch("rmsnorm_rope_kernel");
 }

@@ -2,6 +2,7 @@
 
     python -m kairos_sensenova_b200.profile_cases attn S H   # attention_fp8 on attn_inputs(1, S, H, 128, seed=1)
     python -m kairos_sensenova_b200.profile_cases gdn  T H   # chunk_gated_delta_rule on gdn_inputs(1, T, H, 128, 128, seed=0)
+    python -m kairos_sensenova_b200.profile_cases prologue T H  # gdn_prologue on a fused [T, 3*H*128 + 2H (+pad)] projection
 
 Each runs the operator twice (warm) on synthetic seeded inputs and exits, so an
 ``ncu -k <kernel> -s <n> -c 1`` capture sees a handful of launches of a
@@ -30,8 +31,21 @@ def main(argv):
         q, k, v, g, beta = gdn_inputs(1, n, h, 128, 128, seed=0)
         for _ in range(2):
             chunk_gated_delta_rule(q, k, v, g, beta, output_final_state=True, use_qk_l2norm_in_kernel=True)
+    elif what == 'prologue':
+        from .fused_ops import gdn_prologue
+        gen = torch.Generator(device='cuda')
+        gen.manual_seed(0)
+        C = (3 * h * 128 + 2 * h + 7) // 8 * 8
+        proj = torch.randn(n, C, generator=gen, device='cuda').to(torch.bfloat16)
+        w = torch.rand(h * 128, 4, generator=gen, device='cuda') - 0.5
+        A_log, dtb = torch.zeros(h, device='cuda'), torch.zeros(h, device='cuda')
+        s = lambda i: proj[:, i * h * 128:(i + 1) * h * 128]  # noqa: E731
+        ab = 3 * h * 128
+        for _ in range(2):
+            gdn_prologue(s(0), s(1), s(2), proj[:, ab:ab + h], proj[:, ab + h:ab + 2 * h], w, w, w, A_log, dtb,
+                         h, 1, n)
     else:
-        raise SystemExit(f'unknown case {what!r} (attn | gdn)')
+        raise SystemExit(f'unknown case {what!r} (attn | gdn | prologue)')
     torch.cuda.synchronize()
     print('ok')
 
