@@ -104,8 +104,9 @@ int kb200_rmsnorm_rope(const void* x, void* y, int64_t rows, int64_t dim, int64_
                        const float* cos_sin, float eps, void* stream);
 
 /* ---------------------------------------------------------------------
- * Softmax attention with FP8-e4m3 Q/K/V, per-(batch, head) amax scaling
- * (scale = amax/448), fp32 softmax and accumulation, bf16 output.
+ * Softmax attention with FP8-e4m3 Q/K (per-(batch, head) amax scaling,
+ * scale = amax/448), fp32 scores and softmax, bf16 probabilities times the
+ * bf16 V for the P.V product (fp32 accumulation), bf16 output.
  * Replaces the attention core called by AttentionModule.forward
  *   kairos/modules/dits/kairos_dit.py:367-373 (module)
  *   kairos/modules/dits/kairos_dit.py:232-277 (flash_attention dispatcher;
@@ -113,31 +114,27 @@ int kb200_rmsnorm_rope(const void* x, void* y, int64_t rows, int64_t dim, int64_
  * q, k, v: [B, S, H*D] bf16 rows, `row_stride` elements apart (0 = H*D, i.e.
  * contiguous; larger when q/k/v are column slices of one fused projection);
  * o: [B, S, H*D] bf16 contiguous; D = 128.
- * two_term = 1 adds a second e4m3 term (the rounding residual, same per-head
- * scale) to q and to v, which doubles the tensor-core work and lifts the
- * cosine similarity to the bf16 reference from ~0.9986 to ~0.9993 on
- * N(0,1) inputs; two_term = 0 is the plain single-term e4m3 path.
+ * Cosine similarity to the bf16 reference ~0.9992 on N(0,1) inputs (e4m3 P
+ * and V as well would bound it near 0.9986).
  * --------------------------------------------------------------------- */
-size_t kb200_attn_fp8_workspace_size(int64_t B, int64_t S, int64_t H, int64_t D, int two_term);
+size_t kb200_attn_fp8_workspace_size(int64_t B, int64_t S, int64_t H, int64_t D);
 int kb200_attn_fp8_fwd(const void* q, const void* k, const void* v, void* o, int64_t B, int64_t S,
-                       int64_t H, int64_t D, int64_t row_stride, float softmax_scale, int two_term,
+                       int64_t H, int64_t D, int64_t row_stride, float softmax_scale,
                        void* workspace, size_t workspace_bytes, void* stream);
 /* The two halves of kb200_attn_fp8_fwd, for callers that time or overlap them
- * separately: _quantize fills the workspace (amax, e4m3 q/k/v^T), _attend reads
- * it and writes o.  Same arguments; _attend must follow a _quantize of the
- * same inputs into the same workspace on the same stream. */
+ * separately: _quantize fills the workspace (amax, e4m3 q/k, bf16 v^T, row
+ * norms), _attend reads it and writes o.  Same arguments; _attend must follow a
+ * _quantize of the same inputs into the same workspace on the same stream. */
 int kb200_attn_fp8_quantize(const void* q, const void* k, const void* v, void* o, int64_t B,
                             int64_t S, int64_t H, int64_t D, int64_t row_stride,
-                            float softmax_scale, int two_term, void* workspace,
-                            size_t workspace_bytes, void* stream);
+                            float softmax_scale, void* workspace, size_t workspace_bytes, void* stream);
 int kb200_attn_fp8_attend(const void* q, const void* k, const void* v, void* o, int64_t B,
                           int64_t S, int64_t H, int64_t D, int64_t row_stride, float softmax_scale,
-                          int two_term, void* workspace, size_t workspace_bytes, void* stream);
+                          void* workspace, size_t workspace_bytes, void* stream);
 /* Synchronises `stream` and reports KB200_ERR_TIMEOUT if a bounded device-side
  * wait of the last attention launch on `workspace` gave up (the kernel then
  * skipped its remaining work instead of hanging). */
-int kb200_attn_fp8_status(const void* workspace, int64_t B, int64_t S, int64_t H, int two_term,
-                          void* stream);
+int kb200_attn_fp8_status(const void* workspace, int64_t B, int64_t S, int64_t H, void* stream);
 
 /* ---------------------------------------------------------------------
  * GatedDeltaNet prologue in one launch: short causal depthwise convolutions

@@ -51,7 +51,7 @@ class GdnPrologueArgs(ctypes.Structure):
 
 
 _ATTN_SIG = (ctypes.c_int, [ctypes.c_void_p] * 4 + [ctypes.c_int64] * 5 +
-             [ctypes.c_float, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p])
+             [ctypes.c_float, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p])
 
 # name -> (restype, argtypes); every symbol include/kb200.h declares
 SIGNATURES = {
@@ -64,11 +64,11 @@ SIGNATURES = {
                            [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_float, ctypes.c_void_p]),
     'kb200_gdn_noalloc_scratch_bytes': (ctypes.c_size_t, []),
     'kb200_gdn_chunk_fwd_noalloc': (ctypes.c_int, [ctypes.POINTER(GdnArgs), ctypes.c_void_p]),
-    'kb200_attn_fp8_workspace_size': (ctypes.c_size_t, [ctypes.c_int64] * 4 + [ctypes.c_int]),
+    'kb200_attn_fp8_workspace_size': (ctypes.c_size_t, [ctypes.c_int64] * 4),
     'kb200_attn_fp8_fwd': _ATTN_SIG,
     'kb200_attn_fp8_quantize': _ATTN_SIG,
     'kb200_attn_fp8_attend': _ATTN_SIG,
-    'kb200_attn_fp8_status': (ctypes.c_int, [ctypes.c_void_p] + [ctypes.c_int64] * 3 + [ctypes.c_int, ctypes.c_void_p]),
+    'kb200_attn_fp8_status': (ctypes.c_int, [ctypes.c_void_p] + [ctypes.c_int64] * 3 + [ctypes.c_void_p]),
     'kb200_gdn_prologue': (ctypes.c_int, [ctypes.POINTER(GdnPrologueArgs), ctypes.c_void_p]),
     'kb200_rmsnorm_gated': (ctypes.c_int, [ctypes.c_void_p] * 4 + [ctypes.c_int64] * 4 +
                             [ctypes.c_float, ctypes.c_void_p]),

@@ -4,11 +4,10 @@
 with q, k, v ``[B, S, N*D]`` bf16 returns ``[B, S, N*D]`` bf16
 (``kairos/modules/dits/kairos_dit.py:362-373``).  The core is computed by the
 sm_100a kernels behind ``kb200_attn_fp8_fwd``: per-(batch, head) amax scaling
-of q/k/v to e4m3, non-causal softmax(q k^T / sqrt(D)) v with fp32 softmax and
-accumulation.  By default q and v carry a second e4m3 term (the rounding
-residual at the same per-head scale): a single e4m3 term bounds the cosine
-similarity to the bf16 reference near 0.9986 on N(0,1) data, below the 0.999
-contract, and the residual term lifts it to ~0.9993.  Like the reference's
+of q/k to e4m3, non-causal softmax(q k^T / sqrt(D)) v with fp32 softmax and
+accumulation; the P.V half runs on bf16 probabilities and the bf16 V (with P
+and V in e4m3 too, the cosine similarity to the bf16 reference would sit near
+0.9986 on N(0,1) data, below the 0.999 contract; this way it is ~0.9992).  Like the reference's
 quantised backends (``SageAttention3Module``, ``kairos_dit.py:398-420``) it
 raises ``NotImplementedError`` for an ``attn_mask``; it also raises for a
 sliding ``window_size``, which it does not implement.
@@ -22,7 +21,7 @@ from . import _lib
 
 
 def attention_fp8(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, num_heads: int,
-                  softmax_scale: float | None = None, two_term: bool = True,
+                  softmax_scale: float | None = None,
                   events=None, check: bool = False) -> torch.Tensor:
     """q, k, v: [B, S, H*D] (bf16; other float dtypes are converted) -> [B, S, H*D] bf16.
 
@@ -50,13 +49,13 @@ def attention_fp8(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, num_heads: 
             ld = HD
         o = torch.empty(B, S, HD, device=dev, dtype=torch.bfloat16)
         L = _lib.lib()
-        nbytes = L.kb200_attn_fp8_workspace_size(B, S, num_heads, D, int(two_term))
+        nbytes = L.kb200_attn_fp8_workspace_size(B, S, num_heads, D)
         if nbytes == 0:
             raise ValueError(f'attention_fp8: unsupported shape B={B} S={S} H={num_heads} D={D} (D must be 128)')
         ws = torch.empty(nbytes, device=dev, dtype=torch.uint8)
         stream = torch.cuda.current_stream(dev).cuda_stream
         args = (qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), o.data_ptr(), B, S, num_heads, D, ld,
-                float(softmax_scale), int(two_term), ws.data_ptr(), nbytes, stream)
+                float(softmax_scale), ws.data_ptr(), nbytes, stream)
         if events is None:
             _lib.check(L.kb200_attn_fp8_fwd(*args), 'attention_fp8')
         else:
@@ -65,7 +64,7 @@ def attention_fp8(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, num_heads: 
             _lib.check(L.kb200_attn_fp8_attend(*args), 'attention_fp8 attend')
             events[1].record()
         if check:   # synchronises; raises if a bounded device wait gave up
-            _lib.check(L.kb200_attn_fp8_status(ws.data_ptr(), B, S, num_heads, int(two_term), stream),
+            _lib.check(L.kb200_attn_fp8_status(ws.data_ptr(), B, S, num_heads, stream),
                        'attention_fp8')
     return o
 
@@ -73,17 +72,16 @@ def attention_fp8(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, num_heads: 
 class AttentionModule(nn.Module):
     """Drop-in for ``AttentionModule`` / ``SageAttention3Module`` (``kairos_dit.py:362-420``)."""
 
-    def __init__(self, num_heads, two_term: bool = True):
+    def __init__(self, num_heads):
         super().__init__()
         self.num_heads = num_heads
-        self.two_term = two_term
 
     def forward(self, q, k, v, attn_mask=None, window_size=(-1, -1)):
         if attn_mask is not None:
             raise NotImplementedError('FP8 attention path does not support arbitrary attn_mask')
         if tuple(window_size) != (-1, -1):
             raise NotImplementedError('FP8 attention path does not implement windowed attention')
-        return attention_fp8(q, k, v, self.num_heads, two_term=self.two_term)
+        return attention_fp8(q, k, v, self.num_heads)
 
 
 FP8AttentionModule = AttentionModule

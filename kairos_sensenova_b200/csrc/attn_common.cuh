@@ -12,17 +12,15 @@ struct Params {
   const __nv_bfloat16* k;
   const __nv_bfloat16* v;
   __nv_bfloat16* o;
-  uint8_t* q8;   // [B, H, S_pad, D]
-  uint8_t* k8;   // [B, H, S_pad, D]
-  uint8_t* vt8;  // [B, H, D, S_pad]
-  uint8_t* q8r;  // [B, H, S_pad, D]  e4m3 residual q/s - e4m3(q/s)   (two_term only)
-  uint8_t* vt8r; // [B, H, D, S_pad]  e4m3 residual of v             (two_term only)
-  float* amax;   // [3, B, H]
+  uint8_t* q8;   // [B, H, S_pad, D]  e4m3
+  uint8_t* k8;   // [B, H, S_pad, D]  e4m3
+  __nv_bfloat16* vt;  // [B, H, D, S_pad]  V^T, bf16
+  float* amax;   // [2, B, H]           max |q|, max |k| per (batch, head)
+  float* qn;     // [B, H, S_pad]      |q/s_q| per row (before e4m3 rounding)
+  float* kn;     // [B, H, S_pad/64]   max |k/s_k| over each 64-key tile
   int B, S, H, S_pad;
   int64_t ld;    // elements between consecutive tokens of q/k/v (H*D when contiguous)
   float softmax_scale;
-  int vperm;     // 1: permute tokens inside 16-groups of vt8 for the mma.sync fragment order
-  int two_term;  // 1: q and v carry a second e4m3 term (residual, same scale)
   long long* trace;  // optional event timestamps of CTA (0,0) (builds with KB_ATTN_TRACE only)
 };
 
@@ -38,7 +36,7 @@ KB_DEVI float e4m3_to_float(uint8_t b) {
 
 KB_DEVI float scale_of(float amax) { return amax > 0.f ? amax / E4M3_MAX : 1.f; }
 
-// tcgen05 attention launcher (attn_fp8_tc.cu); V^T must be unpermuted (vperm = 0).
+// tcgen05 attention launcher (attn_fp8_tc.cu).
 int launch_attn_tc(const Params& p, int* err, cudaStream_t st);
 
 }  // namespace attn

@@ -40,14 +40,13 @@ def _round8(n):
 
 class HybridBlock:
     def __init__(self, hidden=3072, heads=24, head_dim=128, world=1, rank=0, group=None,
-                 device='cuda', seed=3, conv_size=4, norm_eps=1e-5, two_term=True, grid=(21, 30, 52),
+                 device='cuda', seed=3, conv_size=4, norm_eps=1e-5, grid=(21, 30, 52),
                  attn_eps=1e-6):
         assert heads % world == 0, 'heads must divide evenly over ranks'
         self.hidden, self.H, self.D = hidden, heads, head_dim
         self.P, self.rank, self.group = world, rank, group
         self.Hl = heads // world
         self.eps = norm_eps
-        self.two_term = two_term
         gen = torch.Generator(device=device)
         gen.manual_seed(seed)          # identical weights on every rank
         bf = torch.bfloat16
@@ -152,7 +151,7 @@ class HybridBlock:
                          ld=self.C_attn, heads_per_block=Hl, block_stride=Tl * self.C_attn)
         recv = self._a2a(send).reshape(T, self.C_attn)
         q, k, v = (recv[:, i * Hl * D:(i + 1) * Hl * D].reshape(1, T, Hl * D) for i in range(3))
-        o = attention_fp8(q, k, v, Hl, two_term=self.two_term, events=events)
+        o = attention_fp8(q, k, v, Hl, events=events)
         o_seq = self._head_to_seq(o.reshape(T, Hl * D), Tl)
         return o_seq @ self.AoT
 

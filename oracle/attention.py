@@ -5,10 +5,12 @@
   ``[B,N,S,D]`` and call ``F.scaled_dot_product_attention`` (non-causal, no
   mask, scale D^-1/2), here on CPU in fp32.
 * :func:`fp8_attention_model` -- what the FP8 kernel computes, restated in
-  torch: per-(batch, head) amax scaling of q, k, v to e4m3 (scale = amax/448;
-  q and v optionally with a second e4m3 residual term), softmax in fp32, P
-  rounded to e4m3 after scaling by 2^8 relative to the row max, P V
-  accumulated in fp32.
+  torch: per-(batch, head) amax scaling of q and k to e4m3 (scale = amax/448),
+  scores and softmax in fp32, then either P rounded to bf16 times the bf16 V
+  (``bf16_pv``) or P rounded to e4m3 after scaling by 2^6 relative to the row
+  max times V at its own per-head e4m3 scale; P V accumulated in fp32.
+* :func:`quant_e4m3` optionally adds a second e4m3 term (the rounding
+  residual); the models above do not use it, it measures what such a term buys.
 """
 from __future__ import annotations
 
@@ -48,15 +50,18 @@ def quant_e4m3(x, num_heads, two_term=False):
     return (hi * scale[:, None, :, None]).reshape(B, S, HD), scale
 
 
-def fp8_attention_model(q, k, v, num_heads, two_term=True):
+def fp8_attention_model(q, k, v, num_heads, bf16_pv=True):
     B, S, HD = q.shape
     D = HD // num_heads
-    qd, _ = quant_e4m3(q, num_heads, two_term)
+    qd, _ = quant_e4m3(q, num_heads)
     kd, _ = quant_e4m3(k, num_heads)
-    vd, _ = quant_e4m3(v, num_heads, two_term)
     f = lambda x: x.reshape(B, S, num_heads, D).transpose(1, 2)  # noqa: E731
     s = (f(qd) @ f(kd).transpose(-1, -2)) * D ** -0.5
     m = s.amax(-1, keepdim=True)
-    p = torch.exp(s - m) * 256.0
-    o = (_e4m3(p) @ f(vd)) / p.sum(-1, keepdim=True)
+    p = torch.exp(s - m) * 64.0
+    if bf16_pv:
+        o = (p.bfloat16().float() @ f(v.bfloat16().float())) / p.sum(-1, keepdim=True)
+    else:
+        vd, _ = quant_e4m3(v, num_heads)
+        o = (_e4m3(p) @ f(vd)) / p.sum(-1, keepdim=True)
     return o.transpose(1, 2).reshape(B, S, HD)

@@ -27,9 +27,17 @@ def test_quant_scale_is_per_head_amax():
     assert xd[0, 1, 3] == 896.0 and xd[0, 2, 13] == -2.0
 
 
-def test_two_term_meets_cosine_contract_single_term_does_not():
+def test_bf16_pv_meets_cosine_contract_all_e4m3_does_not():
     g = torch.Generator().manual_seed(1)
     q, k, v = (torch.randn(1, 1024, 256, generator=g).bfloat16() for _ in range(3))
     ref = sdpa_reference(q, k, v, 2)
-    assert _cos(fp8_attention_model(q, k, v, 2, two_term=True), ref) >= 0.999
-    assert _cos(fp8_attention_model(q, k, v, 2, two_term=False), ref) < 0.999
+    assert _cos(fp8_attention_model(q, k, v, 2, bf16_pv=True), ref) >= 0.999
+    assert _cos(fp8_attention_model(q, k, v, 2, bf16_pv=False), ref) < 0.999
+
+
+def test_residual_term_is_the_e4m3_rounding_error():
+    g = torch.Generator().manual_seed(2)
+    x = torch.randn(1, 64, 2 * 128, generator=g)
+    one, s = quant_e4m3(x, 2)
+    two, _ = quant_e4m3(x, 2, two_term=True)
+    assert (two - x).abs().max() < (one - x).abs().max() / 4
