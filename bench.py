@@ -237,7 +237,7 @@ def main():
         fp8_peak = 1.0 / (0.5 / (2 * bf16_tf) + 0.5 / bf16_tf)
         flops = 4.0 * T_FULL * T_FULL * HEAD_DIM * (HEADS // world)
         units = T_FULL * (HEADS // world)
-        traffic = 42.0e6 * units / (8192 * 8) + 2.0 * units * HEAD_DIM
+        traffic = 33.86e6 * units / (8192 * 8) + 2.0 * units * HEAD_DIM
         achieved = flops / (attn_ms * 1e-3) / 1e12
         line = {
             'metric': METRIC, 'value': T_FULL / (step_ms * 1e-3) / 1e6, 'unit': 'Mtokens/s',
@@ -255,7 +255,7 @@ def main():
                          'bound': 'tensor', 'achieved': achieved,
                          'peak': fp8_peak, 'unit': 'TFLOP/s', 'frac': achieved / fp8_peak,
                          'traffic': traffic, 'attn_ms': attn_ms,
-                         'traffic_source': 'ncu dram read bytes of a B1 S8192 H8 capture (42.0 MB) scaled by '
+                         'traffic_source': 'ncu dram read bytes of a B1 S8192 H8 capture (33.86 MB) scaled by '
                                            'tokens x heads, plus the bf16 output bytes',
                          'peak_source': f'{kind} bf16 dense ({bf16_tf} TFLOP/s) x 4/3: QK at 2x (e4m3), PV at 1x (bf16)'},
             'clocks': clocks,
