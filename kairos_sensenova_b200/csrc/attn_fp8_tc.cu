@@ -404,27 +404,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_fp8_tc_kernel(const __grid
   }
 }
 
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  if (!fn) {
-    void* f = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(f);
-  }
-  return fn;
-}
-
 // 2-D map over [rows, cols] elements of `esize` bytes (uint8 or bf16), row pitch `ld`
 // bytes, boxes of 128 bytes x `box_rows` rows, 128-byte swizzle.
 static int make_map(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, uint64_t ld, int esize,
                     int box_rows) {
-  EncodeTiledFn fn = encode_fn();
+  tc::EncodeTiledFn fn = tc::encode_tiled_fn();
   if (!fn) return set_error(KB200_ERR_LAUNCH, "attn_fp8_tc: cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[2] = {cols, rows};
   cuuint64_t strides[1] = {ld};

@@ -18,6 +18,7 @@
 // accumulations are fp32.  Tensor-core work uses mma.sync m16n8k16 bf16.
 #include "common.cuh"
 #include "kb200_internal.h"
+#include "tc_common.cuh"
 #include <type_traits>
 #include <cstring>
 
@@ -386,16 +387,45 @@ __global__ void __launch_bounds__(NTHREADS) gdn_prepare_kernel(Params p) {
 // ---------------------------------------------------------------------------
 constexpr int STATE_THREADS = 256;
 
+#ifdef KB_GDN_TRACE
+__device__ long long g_state_trace[1024 * 8];
+#define STRACE(slot, it) do { if (blockIdx.x == 0 && blockIdx.y == 0 && tid == 0 && (it) < 1024) g_state_trace[(it) * 8 + (slot)] = clock64(); } while (0)
+#else
+#define STRACE(slot, it) do { } while (0)
+#endif
+
 template <int K, int BV>
 struct StateSmem {
-  static constexpr int LDK = K + 8, LDV = BV + 8;
-  __nv_bfloat16 ws[2][BT * LDK];
-  __nv_bfloat16 ks[2][BT * LDK];
+  static constexpr int LDV = BV + 8;
+  // w and k tiles (BT tokens x K) as TMA writes them: K/64 atoms of BT rows x 128 B,
+  // 128-byte swizzle; the struct is placed 1024-byte aligned
+  __nv_bfloat16 ws[2][BT * K];
+  __nv_bfloat16 ks[2][BT * K];
   __nv_bfloat16 us[2][BT * LDV];
   __nv_bfloat16 hb[2][K * LDV];   // bf16 snapshot of the state (B operand of w h)
   __nv_bfloat16 vg[2][BT * LDV];  // gated v_new (B operand of k^T v)
   __nv_bfloat16 vn[BT * LDV];     // v_new staged for coalesced 16-byte stores
   float gcs[2][BT];
+  uint64_t full[2];               // the w and k tiles of buffer b landed (TMA)
+};
+
+// Element (r, c) (c a multiple of 8) of a BT-row tile stored as 64-column SW128 atoms.
+KB_DEVI const __nv_bfloat16* sw128_at(const __nv_bfloat16* base, int r, int c) {
+  return base + (c >> 6) * (BT * 64) + r * 64 + ((((c >> 3) & 7) ^ (r & 7)) << 3);
+}
+// load_a_rowmajor / load_a_transposed for such swizzled tiles
+KB_DEVI void load_a_rowmajor_sw(uint32_t* a, const __nv_bfloat16* base, int r0, int c0, int lane) {
+  ldsm_x4(a[0], a[1], a[2], a[3], sw128_at(base, r0 + (lane & 15), c0 + ((lane >> 4) << 3)));
+}
+KB_DEVI void load_a_transposed_sw(uint32_t* a, const __nv_bfloat16* base, int m0, int k0, int lane) {
+  const int mat = lane >> 3, r = lane & 7;
+  ldsm_x4_t(a[0], a[1], a[2], a[3], sw128_at(base, k0 + ((mat >> 1) << 3) + r, m0 + ((mat & 1) << 3)));
+}
+
+// TMA maps of the w and k tensors ([tokens, H, K] bf16) as 3-D (K, H, tokens),
+// boxes of 64 channels x 1 head x BT tokens.
+struct StateMaps {
+  CUtensorMap w, k;
 };
 
 KB_DEVI void cp_async4(void* smem, const void* gmem, bool pred) {
@@ -418,21 +448,22 @@ struct StateCopyPlan {
   }
 };
 
+// Loads of one chunk into buffer `buf`: thread 0 issues the TMA boxes of the w
+// and k tiles (counted on sm.full[buf]; rows past the chunk end carry the next
+// sequence's rows or zero fill -- finite values that only ever meet zero gates);
+// u rows and the strided gate values go through cp.async with zero fill.
 template <int K, int BV>
-KB_DEVI void state_issue_loads(StateSmem<K, BV>& sm, int buf, const Params& p, const StateCopyPlan<K, BV>& cp,
-                               int t0, int L, int h, int v0, int V, int tid) {
+KB_DEVI void state_issue_loads(StateSmem<K, BV>& sm, const StateMaps& maps, int buf, const Params& p,
+                               const StateCopyPlan<K, BV>& cp, int t0, int L, int h, int v0, int V, int tid) {
   using S = StateSmem<K, BV>;
-  using CP = StateCopyPlan<K, BV>;
-  const size_t HK = (size_t)p.H * K;
-  const __nv_bfloat16* wb = p.w + (size_t)t0 * HK + (size_t)h * K + cp.kc;
-  const __nv_bfloat16* kb = p.kn + (size_t)t0 * HK + (size_t)h * K + cp.kc;
+  if (tid == 0) {
+    // every ldmatrix read of this buffer completed before the block barrier that precedes this call
+    tc::mbar_expect_tx(&sm.full[buf], 2 * BT * K * 2);
 #pragma unroll
-  for (int i = 0; i < CP::KIT; ++i) {
-    const int r = cp.kr0 + i * CP::KRS;
-    const bool ok = r < L;
-    const size_t off = (size_t)(ok ? r : 0) * HK;
-    cp_async16(&sm.ws[buf][r * S::LDK + cp.kc], wb + off, ok);
-    cp_async16(&sm.ks[buf][r * S::LDK + cp.kc], kb + off, ok);
+    for (int a = 0; a < K / 64; ++a) {
+      tc::tma_load_3d(sm.ws[buf] + a * BT * 64, &maps.w, &sm.full[buf], a * 64, h, t0);
+      tc::tma_load_3d(sm.ks[buf] + a * BT * 64, &maps.k, &sm.full[buf], a * 64, h, t0);
+    }
   }
   if (cp.ur < BT) {
     const bool ok = cp.ur < L;
@@ -444,11 +475,12 @@ KB_DEVI void state_issue_loads(StateSmem<K, BV>& sm, int buf, const Params& p, c
 }
 
 template <int K, int V, int BV>
-__global__ void __launch_bounds__(STATE_THREADS) gdn_state_kernel(Params p) {
+__global__ void __launch_bounds__(STATE_THREADS) gdn_state_kernel(Params p, const __grid_constant__ StateMaps maps) {
   static_assert(BV == 32, "state kernel tiles assume BV = 32");
-  extern __shared__ __align__(128) unsigned char smem_raw[];
+  static_assert(K % 64 == 0, "w/k tiles are 64-column swizzled atoms");
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
   using S = StateSmem<K, BV>;
-  S& sm = *reinterpret_cast<S*>(smem_raw);
+  S& sm = *reinterpret_cast<S*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g8 = lane >> 2, t4 = lane & 3;
   const int v0 = blockIdx.x * BV;
@@ -480,12 +512,19 @@ __global__ void __launch_bounds__(STATE_THREADS) gdn_state_kernel(Params p) {
         hacc[m][nn][e] = p.h0 ? p.h0[((size_t)nh * K + r) * V + cc] : 0.f;
       }
   const StateCopyPlan<K, BV> cplan(tid);
-  if (NTn > 0) state_issue_loads<K, BV>(sm, 0, p, cplan, bos, min(BT, Tn), h, v0, V, tid);
+  if (tid == 0) {
+    tc::mbar_init(&sm.full[0], 1);
+    tc::mbar_init(&sm.full[1], 1);
+    tc::fence_barrier_init();
+  }
+  __syncthreads();
+  if (NTn > 0) state_issue_loads<K, BV>(sm, maps, 0, p, cplan, bos, min(BT, Tn), h, v0, V, tid);
   const int rg = warp & 3, c0 = (warp >> 2) * (BV / 2);
 
   for (int it = 0; it < NTn; ++it) {
     const int buf = it & 1;
     const int t0 = bos + it * BT, L = min(BT, Tn - it * BT);
+    STRACE(0, it);
     // (a) snapshot: bf16 state -> smem operand and -> global h[chunk]
     __nv_bfloat16* hg = p.hs + ((size_t)(cbase + it) * H + h) * K * V;
     __nv_bfloat16* hb = sm.hb[buf];
@@ -500,16 +539,23 @@ __global__ void __launch_bounds__(STATE_THREADS) gdn_state_kernel(Params p) {
         *reinterpret_cast<uint32_t*>(&hb[r * S::LDV + cc]) = lo;
         *reinterpret_cast<uint32_t*>(&hb[(r + 8) * S::LDV + cc]) = hi;
       }
+    STRACE(1, it);
     cp_async_wait<0>();
-    __syncthreads();
+    // bounded: on a timeout the pass stops here (outputs of later chunks are
+    // left unwritten) instead of hanging the GPU
+    if (!__syncthreads_and(tc::mbar_wait(&sm.full[buf], (it >> 1) & 1))) break;
+    STRACE(2, it);
+    STRACE(3, it);
     // snapshot -> global h[chunk] as coalesced 16-byte vectors
 #pragma unroll
     for (int i = 0; i < K * (BV / 8) / STATE_THREADS; ++i) {
       const int idx = tid + i * STATE_THREADS, r = idx / (BV / 8), cv = (idx % (BV / 8)) * 8;
       *reinterpret_cast<uint4*>(hg + (size_t)r * V + v0 + cv) = *reinterpret_cast<const uint4*>(&hb[r * S::LDV + cv]);
     }
+    STRACE(7, it);
     if (it + 1 < NTn)
-      state_issue_loads<K, BV>(sm, buf ^ 1, p, cplan, t0 + BT, min(BT, Tn - (it + 1) * BT), h, v0, V, tid);
+      state_issue_loads<K, BV>(sm, maps, buf ^ 1, p, cplan, t0 + BT, min(BT, Tn - (it + 1) * BT), h, v0, V, tid);
+    STRACE(4, it);
     // (b) v_new = u - w h   (rows 16 rg.., columns c0..c0+BV/2); two accumulator sets halve the chain
     const float glast = sm.gcs[buf][L - 1];
     __nv_bfloat16* vg = sm.vg[buf];
@@ -522,9 +568,9 @@ __global__ void __launch_bounds__(STATE_THREADS) gdn_state_kernel(Params p) {
 #pragma unroll
       for (int kk = 0; kk < K; kk += 32) {
         uint32_t a0[4], a1[4], b0[4], b1[4];
-        load_a_rowmajor(a0, sm.ws[buf], S::LDK, rg * 16, kk, lane);
+        load_a_rowmajor_sw(a0, sm.ws[buf], rg * 16, kk, lane);
         load_b_kmajor_rows_x2n(b0, hb, S::LDV, kk, c0, lane);
-        load_a_rowmajor(a1, sm.ws[buf], S::LDK, rg * 16, kk + 16, lane);
+        load_a_rowmajor_sw(a1, sm.ws[buf], rg * 16, kk + 16, lane);
         load_b_kmajor_rows_x2n(b1, hb, S::LDV, kk + 16, c0, lane);
         mma_bf16(acc0[0], a0, b0);
         mma_bf16(acc0[1], a0, b0 + 2);
@@ -549,7 +595,9 @@ __global__ void __launch_bounds__(STATE_THREADS) gdn_state_kernel(Params p) {
         *reinterpret_cast<uint32_t*>(&vg[r1 * S::LDV + cc]) = pack_bf16(a2 * e1, a3 * e1);
       }
     }
+    STRACE(5, it);
     __syncthreads();
+    STRACE(6, it);
     // v_new -> global as 16-byte vectors (rows < L)
     if (cplan.ur < L)
       *reinterpret_cast<uint4*>(p.vnew + ((size_t)(t0 + cplan.ur) * H + h) * V + v0 + cplan.uc) =
@@ -568,7 +616,7 @@ __global__ void __launch_bounds__(STATE_THREADS) gdn_state_kernel(Params p) {
 #pragma unroll
         for (int m = 0; m < MT; ++m) {
           uint32_t a[4];
-          load_a_transposed(a, sm.ks[buf], S::LDK, m0 + m * 16, kk, lane);
+          load_a_transposed_sw(a, sm.ks[buf], m0 + m * 16, kk, lane);
 #pragma unroll
           for (int n0 = 0; n0 < BV; n0 += 16) {
             uint32_t b[4];
@@ -770,6 +818,22 @@ int validate(const KB200GdnArgs* a) {
   return KB200_OK;
 }
 
+// 3-D map (K, H, tokens) of a [tokens, H, K] bf16 tensor: boxes of 64 channels x
+// 1 head x 64 tokens, 128-byte swizzle, zero fill past the last token.
+int state_map(CUtensorMap* m, const void* base, int64_t tokens, int64_t H, int K) {
+  kb::tc::EncodeTiledFn fn = kb::tc::encode_tiled_fn();
+  if (!fn) return kb::set_error(KB200_ERR_LAUNCH, "gdn: cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)H, (cuuint64_t)tokens};
+  cuuint64_t strides[2] = {(cuuint64_t)K * 2, (cuuint64_t)H * K * 2};
+  cuuint32_t box[3] = {64, 1, (cuuint32_t)gdn::BT};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return kb::set_error(KB200_ERR_LAUNCH, "gdn: tensor map encode failed (%d)", (int)r);
+  return KB200_OK;
+}
+
 template <int K, int V>
 int launch(const KB200GdnArgs* a, const WsLayout& L, char* ws, cudaStream_t st) {
   gdn::Params p{};
@@ -805,9 +869,12 @@ int launch(const KB200GdnArgs* a, const WsLayout& L, char* ws, cudaStream_t st) 
     gdn::gdn_prepare_kernel<K, V><<<dim3(nchunks, H), gdn::NTHREADS, s1, st>>>(p);
     if (int e = check_launch("gdn_prepare_kernel")) return e;
   }
-  const size_t s2 = sizeof(gdn::StateSmem<K, BV>);
+  gdn::StateMaps maps;
+  if (int e = state_map(&maps.w, p.w, a->B * a->T, H, K)) return e;
+  if (int e = state_map(&maps.k, p.kn, a->B * a->T, H, K)) return e;
+  const size_t s2 = sizeof(gdn::StateSmem<K, BV>) + 1024;
   cudaFuncSetAttribute(gdn::gdn_state_kernel<K, V, BV>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s2);
-  gdn::gdn_state_kernel<K, V, BV><<<dim3(V / BV, (unsigned)(a->N * H)), gdn::STATE_THREADS, s2, st>>>(p);
+  gdn::gdn_state_kernel<K, V, BV><<<dim3(V / BV, (unsigned)(a->N * H)), gdn::STATE_THREADS, s2, st>>>(p, maps);
   if (int e = check_launch("gdn_state_kernel")) return e;
   if (nchunks > 0) {
     const size_t s3 = sizeof(gdn::OutSmem<K, BVO>);
