@@ -85,6 +85,12 @@ KB_DEVI void load_b_kmajor_rows_x2n(uint32_t* b, const __nv_bfloat16* base, int 
   int nn = n0 + ((mat >> 1) << 3);
   ldsm_x4_t(b[0], b[1], b[2], b[3], base + kk * ld + nn);
 }
+// One n-tile of 8 of such a B: b[0..1] -> n-tile n0 (lanes 16-31 repeat 0-15's addresses).
+KB_DEVI void load_b_kmajor_rows_x1n(uint32_t* b, const __nv_bfloat16* base, int ld, int k0, int n0, int lane) {
+  const int kk = k0 + (((lane >> 3) & 1) << 3) + (lane & 7);
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];\n"
+               : "=r"(b[0]), "=r"(b[1]) : "r"(smem_u32(base + kk * ld + n0)));
+}
 // B given as N x K row-major storage (element (k, n) at base[n*ld + k]); two n-tiles.
 KB_DEVI void load_b_nmajor_rows_x2n(uint32_t* b, const __nv_bfloat16* base, int ld, int k0, int n0,
                                     int lane) {

@@ -476,7 +476,7 @@ KB_DEVI void state_issue_loads(StateSmem<K, BV>& sm, const StateMaps& maps, int 
 
 template <int K, int V, int BV>
 __global__ void __launch_bounds__(STATE_THREADS) gdn_state_kernel(Params p, const __grid_constant__ StateMaps maps) {
-  static_assert(BV == 32, "state kernel tiles assume BV = 32");
+  static_assert(BV == 16 || BV == 32, "state kernel tiles assume BV = 16 or 32");
   static_assert(K % 64 == 0, "w/k tiles are 64-column swizzled atoms");
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   using S = StateSmem<K, BV>;
@@ -560,28 +560,35 @@ __global__ void __launch_bounds__(STATE_THREADS) gdn_state_kernel(Params p, cons
     const float glast = sm.gcs[buf][L - 1];
     __nv_bfloat16* vg = sm.vg[buf];
     {
-      float acc0[2][4], acc1[2][4];
+      constexpr int NBW = BV / 16;   // n-tiles of 8 per warp
+      float acc0[NBW][4], acc1[NBW][4];
 #pragma unroll
-      for (int nn = 0; nn < 2; ++nn)
+      for (int nn = 0; nn < NBW; ++nn)
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc0[nn][e] = acc1[nn][e] = 0.f;
 #pragma unroll
       for (int kk = 0; kk < K; kk += 32) {
-        uint32_t a0[4], a1[4], b0[4], b1[4];
+        uint32_t a0[4], a1[4], b0[2 * NBW], b1[2 * NBW];
         load_a_rowmajor_sw(a0, sm.ws[buf], rg * 16, kk, lane);
-        load_b_kmajor_rows_x2n(b0, hb, S::LDV, kk, c0, lane);
         load_a_rowmajor_sw(a1, sm.ws[buf], rg * 16, kk + 16, lane);
-        load_b_kmajor_rows_x2n(b1, hb, S::LDV, kk + 16, c0, lane);
-        mma_bf16(acc0[0], a0, b0);
-        mma_bf16(acc0[1], a0, b0 + 2);
-        mma_bf16(acc1[0], a1, b1);
-        mma_bf16(acc1[1], a1, b1 + 2);
+        if constexpr (NBW == 2) {
+          load_b_kmajor_rows_x2n(b0, hb, S::LDV, kk, c0, lane);
+          load_b_kmajor_rows_x2n(b1, hb, S::LDV, kk + 16, c0, lane);
+        } else {
+          load_b_kmajor_rows_x1n(b0, hb, S::LDV, kk, c0, lane);
+          load_b_kmajor_rows_x1n(b1, hb, S::LDV, kk + 16, c0, lane);
+        }
+#pragma unroll
+        for (int nn = 0; nn < NBW; ++nn) {
+          mma_bf16(acc0[nn], a0, b0 + 2 * nn);
+          mma_bf16(acc1[nn], a1, b1 + 2 * nn);
+        }
       }
       const int r0 = rg * 16 + g8, r1 = r0 + 8;
       const float e0 = (r0 < L) ? __expf(glast - sm.gcs[buf][r0]) : 0.f;
       const float e1 = (r1 < L) ? __expf(glast - sm.gcs[buf][r1]) : 0.f;
 #pragma unroll
-      for (int nn = 0; nn < 2; ++nn) {
+      for (int nn = 0; nn < NBW; ++nn) {
         const int cc = c0 + nn * 8 + 2 * t4;
         const __nv_bfloat162 u0 = *reinterpret_cast<const __nv_bfloat162*>(&sm.us[buf][r0 * S::LDV + cc]);
         const __nv_bfloat162 u1 = *reinterpret_cast<const __nv_bfloat162*>(&sm.us[buf][r1 * S::LDV + cc]);
@@ -834,6 +841,32 @@ int state_map(CUtensorMap* m, const void* base, int64_t tokens, int64_t H, int K
   return KB200_OK;
 }
 
+// State-pass V-slice width: 0 = chosen from the grid size, 16 or 32 forced by the
+// KB200_GDN_STATE_BV environment variable (a tuning knob, read once).
+int state_bv() {
+  static const int bv = [] {
+    const char* s = getenv("KB200_GDN_STATE_BV");
+    const int v = s ? atoi(s) : 0;
+    return (v == 16 || v == 32) ? v : 0;
+  }();
+  return bv;
+}
+
+int sm_count() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+template <int K, int V, int BV>
+int launch_state(const gdn::Params& p, const gdn::StateMaps& maps, unsigned nh, cudaStream_t st) {
+  const size_t s2 = sizeof(gdn::StateSmem<K, BV>) + 1024;
+  cudaFuncSetAttribute(gdn::gdn_state_kernel<K, V, BV>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s2);
+  gdn::gdn_state_kernel<K, V, BV><<<dim3(V / BV, nh), gdn::STATE_THREADS, s2, st>>>(p, maps);
+  return check_launch("gdn_state_kernel");
+}
+
 template <int K, int V>
 int launch(const KB200GdnArgs* a, const WsLayout& L, char* ws, cudaStream_t st) {
   gdn::Params p{};
@@ -872,10 +905,17 @@ int launch(const KB200GdnArgs* a, const WsLayout& L, char* ws, cudaStream_t st) 
   gdn::StateMaps maps;
   if (int e = state_map(&maps.w, p.w, a->B * a->T, H, K)) return e;
   if (int e = state_map(&maps.k, p.kn, a->B * a->T, H, K)) return e;
-  const size_t s2 = sizeof(gdn::StateSmem<K, BV>) + 1024;
-  cudaFuncSetAttribute(gdn::gdn_state_kernel<K, V, BV>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s2);
-  gdn::gdn_state_kernel<K, V, BV><<<dim3(V / BV, (unsigned)(a->N * H)), gdn::STATE_THREADS, s2, st>>>(p, maps);
-  if (int e = check_launch("gdn_state_kernel")) return e;
+  // The state pass is a chain of dependent chunk steps; its time is the latency of
+  // one step times the chunk count.  Narrower V slices shorten each step and put
+  // more CTAs on the SMs, so they are used when the 16-wide grid still fits one
+  // CTA per SM (few heads, e.g. one Ulysses rank's share).  Measured on B200 at
+  // T 32760: H 24 1.69 ms (32) vs 1.81 (16); H 12 1.18 vs 1.10; H 3 0.78 vs 0.67.
+  const long ctas32 = (long)(V / 32) * a->N * H;
+  if (state_bv() == 16 || (state_bv() == 0 && 2 * ctas32 <= sm_count())) {
+    if (int e = launch_state<K, V, 16>(p, maps, (unsigned)(a->N * H), st)) return e;
+  } else {
+    if (int e = launch_state<K, V, BV>(p, maps, (unsigned)(a->N * H), st)) return e;
+  }
   if (nchunks > 0) {
     const size_t s3 = sizeof(gdn::OutSmem<K, BVO>);
     cudaFuncSetAttribute(gdn::gdn_output_kernel<K, V, BVO>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s3);
