@@ -21,6 +21,7 @@
 #include "tc_common.cuh"
 #include <type_traits>
 #include <cstring>
+#include <algorithm>
 
 namespace kb {
 namespace gdn {
@@ -51,6 +52,16 @@ struct Params {
   int T, H, NT;       // NT = chunks per sequence when cu_seqlens == nullptr
   float scale;
   int l2norm;
+  // Segmented state pass (fixed-length sequences only): each sequence's chunks are
+  // split into nseg segments of seg_chunks.  seg_mode 1 runs every segment but the
+  // last from a zero state (seg_b: its end state) and, in the extra CTAs of grid.x,
+  // from identity columns with u = 0 (seg_m: the segment's transition, stored
+  // transposed); seg_mode 2 runs every segment from its start state (seg_h, written
+  // by the combine kernel) and writes the snapshots, v_new and the final state.
+  int seg_mode, nseg, seg_chunks;
+  float* seg_b;       // [N*H, nseg, K, V]
+  float* seg_m;       // [N*H, nseg, K(col), K(row)]
+  float* seg_h;       // [N*H, nseg, K, V]
 };
 
 // Warp-level 16x16 fp32 product: C = +-(A B [+ C]), row-major operands with
@@ -454,7 +465,8 @@ struct StateCopyPlan {
 // u rows and the strided gate values go through cp.async with zero fill.
 template <int K, int BV>
 KB_DEVI void state_issue_loads(StateSmem<K, BV>& sm, const StateMaps& maps, int buf, const Params& p,
-                               const StateCopyPlan<K, BV>& cp, int t0, int L, int h, int v0, int V, int tid) {
+                               const StateCopyPlan<K, BV>& cp, int t0, int L, int h, int v0, int V, int tid,
+                               bool load_u) {
   using S = StateSmem<K, BV>;
   if (tid == 0) {
     // every ldmatrix read of this buffer completed before the block barrier that precedes this call
@@ -465,7 +477,7 @@ KB_DEVI void state_issue_loads(StateSmem<K, BV>& sm, const StateMaps& maps, int 
       tc::tma_load_3d(sm.ks[buf] + a * BT * 64, &maps.k, &sm.full[buf], a * 64, h, t0);
     }
   }
-  if (cp.ur < BT) {
+  if (load_u && cp.ur < BT) {
     const bool ok = cp.ur < L;
     cp_async16(&sm.us[buf][cp.ur * S::LDV + cp.uc],
                p.u + ((size_t)(t0 + (ok ? cp.ur : 0)) * p.H + h) * V + v0 + cp.uc, ok);
@@ -483,8 +495,14 @@ __global__ void __launch_bounds__(STATE_THREADS) gdn_state_kernel(Params p, cons
   S& sm = *reinterpret_cast<S*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g8 = lane >> 2, t4 = lane & 3;
-  const int v0 = blockIdx.x * BV;
-  const int nh = blockIdx.y, n = nh / p.H, h = nh % p.H, H = p.H;
+  const int nseg = p.seg_mode ? p.nseg : 1;
+  const int nh = blockIdx.y / nseg, seg = blockIdx.y % nseg, n = nh / p.H, h = nh % p.H, H = p.H;
+  // transition CTA of the segmented local pass: columns mcol0.. of the K x K transition
+  const bool trans = p.seg_mode == 1 && (int)blockIdx.x >= V / BV;
+  const int v0 = trans ? 0 : blockIdx.x * BV;
+  const int mcol0 = trans ? ((int)blockIdx.x - V / BV) * BV : 0;
+  // the local pass needs no end state of the last segment and no transition of the first
+  if (p.seg_mode == 1 && (seg == nseg - 1 || (trans && seg == 0))) return;
   int bos, Tn, cbase;
   if (p.cu_seqlens) {
     bos = p.cu_seqlens[n];
@@ -496,6 +514,9 @@ __global__ void __launch_bounds__(STATE_THREADS) gdn_state_kernel(Params p, cons
     cbase = n * p.NT;
   }
   const int NTn = (Tn + BT - 1) / BT;
+  const int it0 = p.seg_mode ? seg * p.seg_chunks : 0;
+  const int it1 = p.seg_mode ? min(NTn, it0 + p.seg_chunks) : NTn;
+  const bool seg_start0 = p.seg_mode != 0 && seg > 0;   // this run does not start at the sequence start
   constexpr int RW = K / 8;        // state rows per warp
   constexpr int MT = RW / 16;      // m-tiles per warp
   constexpr int NB = BV / 8;       // n-tiles of the state
@@ -509,7 +530,14 @@ __global__ void __launch_bounds__(STATE_THREADS) gdn_state_kernel(Params p, cons
       for (int e = 0; e < 4; ++e) {
         const int r = m0 + m * 16 + g8 + ((e >> 1) << 3);
         const int cc = v0 + nn * 8 + 2 * t4 + (e & 1);
-        hacc[m][nn][e] = p.h0 ? p.h0[((size_t)nh * K + r) * V + cc] : 0.f;
+        float init;
+        if (trans)
+          init = (r == mcol0 + nn * 8 + 2 * t4 + (e & 1)) ? 1.f : 0.f;
+        else if (seg_start0)
+          init = p.seg_mode == 2 ? p.seg_h[(((size_t)nh * nseg + seg) * K + r) * V + cc] : 0.f;
+        else
+          init = p.h0 ? p.h0[((size_t)nh * K + r) * V + cc] : 0.f;
+        hacc[m][nn][e] = init;
       }
   const StateCopyPlan<K, BV> cplan(tid);
   if (tid == 0) {
@@ -517,12 +545,17 @@ __global__ void __launch_bounds__(STATE_THREADS) gdn_state_kernel(Params p, cons
     tc::mbar_init(&sm.full[1], 1);
     tc::fence_barrier_init();
   }
+  if (trans)   // u = 0 for the transition: its tiles are never loaded
+    for (int i = tid; i < 2 * BT * S::LDV; i += STATE_THREADS) (&sm.us[0][0])[i] = __float2bfloat16(0.f);
   __syncthreads();
-  if (NTn > 0) state_issue_loads<K, BV>(sm, maps, 0, p, cplan, bos, min(BT, Tn), h, v0, V, tid);
+  if (it1 > it0)
+    state_issue_loads<K, BV>(sm, maps, 0, p, cplan, bos + it0 * BT, min(BT, Tn - it0 * BT), h, v0, V, tid,
+                             !trans);
   const int rg = warp & 3, c0 = (warp >> 2) * (BV / 2);
 
-  for (int it = 0; it < NTn; ++it) {
-    const int buf = it & 1;
+  const bool write_seq = p.seg_mode != 1;   // snapshots and v_new are written by the final pass only
+  for (int it = it0; it < it1; ++it) {
+    const int li = it - it0, buf = li & 1;
     const int t0 = bos + it * BT, L = min(BT, Tn - it * BT);
     STRACE(0, it);
     // (a) snapshot: bf16 state -> smem operand and -> global h[chunk]
@@ -543,18 +576,19 @@ __global__ void __launch_bounds__(STATE_THREADS) gdn_state_kernel(Params p, cons
     cp_async_wait<0>();
     // bounded: on a timeout the pass stops here (outputs of later chunks are
     // left unwritten) instead of hanging the GPU
-    if (!__syncthreads_and(tc::mbar_wait(&sm.full[buf], (it >> 1) & 1))) break;
+    if (!__syncthreads_and(tc::mbar_wait(&sm.full[buf], (li >> 1) & 1))) break;
     STRACE(2, it);
     STRACE(3, it);
     // snapshot -> global h[chunk] as coalesced 16-byte vectors
 #pragma unroll
-    for (int i = 0; i < K * (BV / 8) / STATE_THREADS; ++i) {
+    for (int i = 0; i < (write_seq ? K * (BV / 8) / STATE_THREADS : 0); ++i) {
       const int idx = tid + i * STATE_THREADS, r = idx / (BV / 8), cv = (idx % (BV / 8)) * 8;
       *reinterpret_cast<uint4*>(hg + (size_t)r * V + v0 + cv) = *reinterpret_cast<const uint4*>(&hb[r * S::LDV + cv]);
     }
     STRACE(7, it);
-    if (it + 1 < NTn)
-      state_issue_loads<K, BV>(sm, maps, buf ^ 1, p, cplan, t0 + BT, min(BT, Tn - (it + 1) * BT), h, v0, V, tid);
+    if (it + 1 < it1)
+      state_issue_loads<K, BV>(sm, maps, buf ^ 1, p, cplan, t0 + BT, min(BT, Tn - (it + 1) * BT), h, v0, V, tid,
+                               !trans);
     STRACE(4, it);
     // (b) v_new = u - w h   (rows 16 rg.., columns c0..c0+BV/2); two accumulator sets halve the chain
     const float glast = sm.gcs[buf][L - 1];
@@ -606,7 +640,7 @@ __global__ void __launch_bounds__(STATE_THREADS) gdn_state_kernel(Params p, cons
     __syncthreads();
     STRACE(6, it);
     // v_new -> global as 16-byte vectors (rows < L)
-    if (cplan.ur < L)
+    if (write_seq && cplan.ur < L)
       *reinterpret_cast<uint4*>(p.vnew + ((size_t)(t0 + cplan.ur) * H + h) * V + v0 + cplan.uc) =
           *reinterpret_cast<const uint4*>(&sm.vn[cplan.ur * S::LDV + cplan.uc]);
     // (c) h <- e^{g_last} h + k^T vg
@@ -635,7 +669,12 @@ __global__ void __launch_bounds__(STATE_THREADS) gdn_state_kernel(Params p, cons
       }
     }
   }
-  if (p.ht) {
+  float* dst = nullptr;
+  if (p.seg_mode == 1)
+    dst = trans ? p.seg_m + ((size_t)nh * nseg + seg) * K * K : p.seg_b + ((size_t)nh * nseg + seg) * K * V;
+  else if (p.ht && (p.seg_mode == 0 || seg == nseg - 1))
+    dst = p.ht + (size_t)nh * K * V;
+  if (dst) {
 #pragma unroll
     for (int m = 0; m < MT; ++m)
 #pragma unroll
@@ -643,9 +682,72 @@ __global__ void __launch_bounds__(STATE_THREADS) gdn_state_kernel(Params p, cons
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int r = m0 + m * 16 + g8 + ((e >> 1) << 3);
-          const int cc = v0 + nn * 8 + 2 * t4 + (e & 1);
-          p.ht[((size_t)nh * K + r) * V + cc] = hacc[m][nn][e];
+          const int c = nn * 8 + 2 * t4 + (e & 1);
+          if (trans)
+            dst[(size_t)(mcol0 + c) * K + r] = hacc[m][nn][e];
+          else
+            dst[(size_t)r * V + v0 + c] = hacc[m][nn][e];
         }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Kernel 2b: segment combine.  Grid (V / 32, N * H); 256 threads.  Start states
+// of the segments of one sequence, a short sequential scan in fp32:
+//   h_1 = B_0,  h_s = M_{s-1} h_{s-1} + B_{s-1}   (s = 2 .. nseg-1)
+// (B_0 already starts from the initial state).  Thread t owns rows
+// (t / 8) * RPT .. + RPT and columns 4 (t % 8) .. + 4 of the 32-column slice; the
+// transposed transition streams through shared memory 32 rows of k at a time.
+// ---------------------------------------------------------------------------
+constexpr int COMB_THREADS = 256, COMB_KB = 32;
+
+template <int K, int V>
+__global__ void __launch_bounds__(COMB_THREADS) gdn_seg_combine_kernel(Params p) {
+  constexpr int RPT = K / 32;
+  extern __shared__ __align__(16) float csm[];
+  float* hs = csm;                   // [K][32] current start state slice
+  float* mt = csm + K * 32;          // [COMB_KB][K] rows of M^T
+  const int nh = blockIdx.y, v0 = blockIdx.x * 32, tid = threadIdx.x;
+  const int nseg = p.nseg, r0 = (tid >> 3) * RPT, c0 = (tid & 7) * 4;
+  const size_t sKV = (size_t)K * V;
+  const float* B = p.seg_b + (size_t)nh * nseg * sKV;
+  const float* M = p.seg_m + (size_t)nh * nseg * K * K;
+  float* Hs = p.seg_h + (size_t)nh * nseg * sKV;
+  float acc[RPT][4];
+  for (int s = 1; s < nseg; ++s) {
+#pragma unroll
+    for (int i = 0; i < RPT; ++i) {
+      const float4 b = *reinterpret_cast<const float4*>(B + (size_t)(s - 1) * sKV + (size_t)(r0 + i) * V + v0 + c0);
+      acc[i][0] = b.x; acc[i][1] = b.y; acc[i][2] = b.z; acc[i][3] = b.w;
+    }
+    if (s > 1) {
+      const float* Ms = M + (size_t)(s - 1) * K * K;
+      for (int kb = 0; kb < K; kb += COMB_KB) {
+        __syncthreads();
+        for (int i = tid * 4; i < COMB_KB * K; i += COMB_THREADS * 4)
+          *reinterpret_cast<float4*>(mt + i) = *reinterpret_cast<const float4*>(Ms + (size_t)kb * K + i);
+        __syncthreads();
+#pragma unroll 4
+        for (int k = 0; k < COMB_KB; ++k) {
+          const float4 hv = *reinterpret_cast<const float4*>(hs + (kb + k) * 32 + c0);
+#pragma unroll
+          for (int i = 0; i < RPT; ++i) {
+            const float a = mt[k * K + r0 + i];
+            acc[i][0] = fmaf(a, hv.x, acc[i][0]);
+            acc[i][1] = fmaf(a, hv.y, acc[i][1]);
+            acc[i][2] = fmaf(a, hv.z, acc[i][2]);
+            acc[i][3] = fmaf(a, hv.w, acc[i][3]);
+          }
+        }
+      }
+    }
+    __syncthreads();   // every read of hs of the previous step is done
+#pragma unroll
+    for (int i = 0; i < RPT; ++i) {
+      const float4 o = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+      *reinterpret_cast<float4*>(hs + (r0 + i) * 32 + c0) = o;
+      *reinterpret_cast<float4*>(Hs + (size_t)s * sKV + (size_t)(r0 + i) * V + v0 + c0) = o;
+    }
   }
 }
 
@@ -780,7 +882,60 @@ __global__ void __launch_bounds__(NTHREADS) gdn_output_kernel(Params p) {
 namespace {
 using namespace kb;
 
-struct WsLayout { size_t qn, kn, gc, w, u, vnew, hs, total; };
+// State-pass V-slice width: 0 = chosen from the grid size, 16 or 32 forced by the
+// KB200_GDN_STATE_BV environment variable (a tuning knob, read once).
+int state_bv() {
+  static const int bv = [] {
+    const char* s = getenv("KB200_GDN_STATE_BV");
+    const int v = s ? atoi(s) : 0;
+    return (v == 16 || v == 32) ? v : 0;
+  }();
+  return bv;
+}
+
+int sm_count() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+
+// How the state pass runs: V-slice width and segment count.
+//
+// The pass is a chain of dependent chunk steps; its time is the latency of one
+// step times the chunk count.  Narrower V slices shorten each step and put more
+// CTAs on the SMs, so they are used when the 16-wide grid still fits one CTA per
+// SM (few heads, e.g. one Ulysses rank's share).  Measured on B200 at T 32760:
+// H 24 1.69 ms (32) vs 1.81 (16); H 12 1.18 vs 1.10; H 3 0.78 vs 0.67.
+//
+// When even that leaves SMs idle, the chunks of each (fixed-length) sequence
+// are split into segments that run concurrently: a local pass per segment from
+// a zero state plus its K x K transition (K/BV more CTAs per segment), a short
+// fp32 scan over the segments, then the final pass from each segment's start
+// state.  Segments are sized so the local pass holds at most two CTAs per SM
+// and each segment has at least 16 chunks.  KB200_GDN_SEGMENTS forces a count.
+struct StatePlan { int bv, nseg, seg_chunks; };
+
+StatePlan state_plan(const KB200GdnArgs* a) {
+  StatePlan s{32, 1, 0};
+  const long nh = (long)a->N * a->H;
+  const int sms = sm_count();
+  if (state_bv() == 16 || (state_bv() == 0 && 2 * (a->V / 32) * nh <= sms)) s.bv = 16;
+  if (a->cu_seqlens) return s;
+  const long nt = (a->T + gdn::BT - 1) / gdn::BT;
+  long cap = std::max(1L, 2L * sms / (nh * ((a->V + a->K) / s.bv)));
+  if (const char* e = getenv("KB200_GDN_SEGMENTS")) cap = std::max(1, atoi(e));
+  long nseg = std::min(std::min(cap, nt / 16), 32L);
+  if (nseg > 1) {
+    s.seg_chunks = (int)((nt + nseg - 1) / nseg);
+    s.nseg = (int)((nt + s.seg_chunks - 1) / s.seg_chunks);
+  }
+  if (s.nseg < 2) { s.nseg = 1; s.seg_chunks = 0; }
+  return s;
+}
+
+struct WsLayout { size_t qn, kn, gc, w, u, vnew, hs, seg_b, seg_m, seg_h, total; StatePlan sp; };
 
 WsLayout ws_layout(const KB200GdnArgs* a) {
   const size_t TT = (size_t)a->B * a->T, H = a->H, K = a->K, V = a->V;
@@ -795,6 +950,11 @@ WsLayout ws_layout(const KB200GdnArgs* a) {
   L.u = take(TT * H * V * 2);
   L.vnew = take(TT * H * V * 2);
   L.hs = take((size_t)a->num_chunks * H * K * V * 2);
+  L.sp = state_plan(a);
+  const size_t segs = L.sp.nseg > 1 ? (size_t)a->N * H * L.sp.nseg : 0;
+  L.seg_b = take(segs * K * V * 4);
+  L.seg_m = take(segs * K * K * 4);
+  L.seg_h = take(segs * K * V * 4);
   L.total = off;
   return L;
 }
@@ -841,29 +1001,26 @@ int state_map(CUtensorMap* m, const void* base, int64_t tokens, int64_t H, int K
   return KB200_OK;
 }
 
-// State-pass V-slice width: 0 = chosen from the grid size, 16 or 32 forced by the
-// KB200_GDN_STATE_BV environment variable (a tuning knob, read once).
-int state_bv() {
-  static const int bv = [] {
-    const char* s = getenv("KB200_GDN_STATE_BV");
-    const int v = s ? atoi(s) : 0;
-    return (v == 16 || v == 32) ? v : 0;
-  }();
-  return bv;
-}
-
-int sm_count() {
-  int dev = 0, n = 0;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-  return n > 0 ? n : 148;
-}
-
 template <int K, int V, int BV>
-int launch_state(const gdn::Params& p, const gdn::StateMaps& maps, unsigned nh, cudaStream_t st) {
+int launch_state(gdn::Params p, const gdn::StateMaps& maps, const StatePlan& sp, unsigned nh, cudaStream_t st) {
   const size_t s2 = sizeof(gdn::StateSmem<K, BV>) + 1024;
   cudaFuncSetAttribute(gdn::gdn_state_kernel<K, V, BV>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s2);
-  gdn::gdn_state_kernel<K, V, BV><<<dim3(V / BV, nh), gdn::STATE_THREADS, s2, st>>>(p, maps);
+  if (sp.nseg < 2) {
+    p.seg_mode = 0;
+    gdn::gdn_state_kernel<K, V, BV><<<dim3(V / BV, nh), gdn::STATE_THREADS, s2, st>>>(p, maps);
+    return check_launch("gdn_state_kernel");
+  }
+  p.nseg = sp.nseg;
+  p.seg_chunks = sp.seg_chunks;
+  p.seg_mode = 1;
+  gdn::gdn_state_kernel<K, V, BV><<<dim3((V + K) / BV, nh * sp.nseg), gdn::STATE_THREADS, s2, st>>>(p, maps);
+  if (int e = check_launch("gdn_state_kernel (segment-local)")) return e;
+  const size_t sc = (size_t)(K * 32 + gdn::COMB_KB * K) * 4;
+  cudaFuncSetAttribute(gdn::gdn_seg_combine_kernel<K, V>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sc);
+  gdn::gdn_seg_combine_kernel<K, V><<<dim3(V / 32, nh), gdn::COMB_THREADS, sc, st>>>(p);
+  if (int e = check_launch("gdn_seg_combine_kernel")) return e;
+  p.seg_mode = 2;
+  gdn::gdn_state_kernel<K, V, BV><<<dim3(V / BV, nh * sp.nseg), gdn::STATE_THREADS, s2, st>>>(p, maps);
   return check_launch("gdn_state_kernel");
 }
 
@@ -893,6 +1050,9 @@ int launch(const KB200GdnArgs* a, const WsLayout& L, char* ws, cudaStream_t st) 
   p.NT = (int)((a->T + 63) / 64);
   p.scale = a->scale;
   p.l2norm = a->use_qk_l2norm;
+  p.seg_b = (float*)(ws + L.seg_b);
+  p.seg_m = (float*)(ws + L.seg_m);
+  p.seg_h = (float*)(ws + L.seg_h);
   const int H = (int)a->H;
   const int nchunks = (int)a->num_chunks;
   constexpr int BV = 32, BVO = 64;
@@ -905,16 +1065,10 @@ int launch(const KB200GdnArgs* a, const WsLayout& L, char* ws, cudaStream_t st) 
   gdn::StateMaps maps;
   if (int e = state_map(&maps.w, p.w, a->B * a->T, H, K)) return e;
   if (int e = state_map(&maps.k, p.kn, a->B * a->T, H, K)) return e;
-  // The state pass is a chain of dependent chunk steps; its time is the latency of
-  // one step times the chunk count.  Narrower V slices shorten each step and put
-  // more CTAs on the SMs, so they are used when the 16-wide grid still fits one
-  // CTA per SM (few heads, e.g. one Ulysses rank's share).  Measured on B200 at
-  // T 32760: H 24 1.69 ms (32) vs 1.81 (16); H 12 1.18 vs 1.10; H 3 0.78 vs 0.67.
-  const long ctas32 = (long)(V / 32) * a->N * H;
-  if (state_bv() == 16 || (state_bv() == 0 && 2 * ctas32 <= sm_count())) {
-    if (int e = launch_state<K, V, 16>(p, maps, (unsigned)(a->N * H), st)) return e;
+  if (L.sp.bv == 16) {
+    if (int e = launch_state<K, V, 16>(p, maps, L.sp, (unsigned)(a->N * H), st)) return e;
   } else {
-    if (int e = launch_state<K, V, BV>(p, maps, (unsigned)(a->N * H), st)) return e;
+    if (int e = launch_state<K, V, BV>(p, maps, L.sp, (unsigned)(a->N * H), st)) return e;
   }
   if (nchunks > 0) {
     const size_t s3 = sizeof(gdn::OutSmem<K, BVO>);

@@ -114,3 +114,49 @@ def test_gdn_config1_full_size_two_heads_vs_oracle():
         oref, sref = og.gdn_chunk(sl(q), sl(k), sl(v), sl(g), sl(beta), None, None, True, use_qk_l2norm=True)
         assert max_rel(o[:, :, h:h + 1], oref) <= O_TOL
         assert max_rel(s[:, h:h + 1], sref) <= S_TOL
+
+
+def _seg_inputs(T, H, K, V, seed, decay=0.01):
+    gen = torch.Generator().manual_seed(seed)
+    q = torch.nn.functional.normalize(torch.randn(1, T, H, K, generator=gen), dim=-1)
+    k = torch.nn.functional.normalize(torch.randn(1, T, H, K, generator=gen), dim=-1)
+    v = torch.randn(1, T, H, V, generator=gen)
+    beta = torch.sigmoid(torch.randn(1, T, H, generator=gen))
+    g = -torch.nn.functional.softplus(torch.randn(1, T, H, generator=gen)) * decay
+    h0 = torch.randn(1, H, K, V, generator=gen) * 0.1
+    return [x.bfloat16().float() for x in (q, k, v)] + [g, beta.bfloat16().float(), h0]
+
+
+@pytest.mark.parametrize('T,H,K,V', [(4000, 2, 128, 128), (2048, 1, 256, 512)])
+def test_gdn_segmented_state_pass_vs_oracle(T, H, K, V, monkeypatch):
+    """Few heads and a long sequence: the state pass splits the chunks into
+    segments (local passes + transitions, an fp32 scan, a final pass).  Slow
+    decay carries the state across segment boundaries; the result must match
+    the fp32 oracle and the one-segment pass."""
+    from kairos_sensenova_b200 import chunk_gated_delta_rule
+    from oracle import gdn as og
+    q, k, v, g, beta, h0 = _seg_inputs(T, H, K, V, seed=21)
+    oref, sref = og.gdn_chunk(q, k, v, g, beta, None, h0, True, use_qk_l2norm=False)
+    c = lambda x, dt=torch.bfloat16: x.to('cuda', dt)  # noqa: E731
+    args = (c(q), c(k), c(v), c(g, torch.float32), c(beta))
+    o, s = chunk_gated_delta_rule(*args, initial_state=c(h0, torch.float32), output_final_state=True)
+    assert max_rel(o, oref) <= O_TOL and max_rel(s, sref) <= S_TOL
+    monkeypatch.setenv('KB200_GDN_SEGMENTS', '1')
+    o1, s1 = chunk_gated_delta_rule(*args, initial_state=c(h0, torch.float32), output_final_state=True)
+    assert max_rel(o, o1) <= 1e-2 and max_rel(s, s1) <= 5e-3
+
+
+def test_gdn_segmented_rank_share_of_config1():
+    """One Ulysses rank's share of config 1 at 8 GPUs (T=32760, 3 heads), the
+    case the segmented state pass exists for; two heads against the oracle."""
+    from kairos_sensenova_b200 import chunk_gated_delta_rule
+    from kairos_sensenova_b200.inputs import gdn_inputs
+    from oracle import gdn as og
+    q, k, v, g, beta = gdn_inputs(1, 32760, 3, 128, 128, seed=0, device='cuda')
+    o, s = chunk_gated_delta_rule(q, k, v, g, beta, output_final_state=True, use_qk_l2norm_in_kernel=True)
+    torch.cuda.synchronize()
+    for h in (0, 2):
+        sl = lambda x: x[:, :, h:h + 1].float().cpu()  # noqa: E731
+        oref, sref = og.gdn_chunk(sl(q), sl(k), sl(v), sl(g), sl(beta), None, None, True, use_qk_l2norm=True)
+        assert max_rel(o[:, :, h:h + 1], oref) <= O_TOL
+        assert max_rel(s[:, h:h + 1], sref) <= S_TOL
