@@ -7,7 +7,11 @@ sequence-parallel over N GPUs (one process per GPU, NCCL).  Metric: hybrid
 block Mtokens/s = T / step time.  Synthetic seeded N(0,1) hidden states
 [32760, 3072] bf16, random-init N(0,0.02) weights (no checkpoints exist here).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--dit-steps K2]
+
+After the hybrid block the same run times BASELINE config 4, the full DiT
+denoise step (``kairos_sensenova_b200.dit``), and adds it to the JSON line as
+``dit_step`` (ms per step, max over ranks; ``--dit-steps 0`` skips it).
 
 For N > 1 launch with torch.distributed.run (127.0.0.1 rendezvous).
 ``--impl reference`` times the reference path's CPU restatement (the oracle
@@ -135,6 +139,49 @@ def run_reference(args, rank):
     print(json.dumps(line), flush=True)
 
 
+def time_dit(args, world, rank, sync_all, flush):
+    """one full DiT denoise step (30 blocks, hidden 3072, 24x128
+    heads, FFN 8192, GDN in 3 of every 4 blocks, FP8 attention in every 4th,
+    cross-attention to 512 text tokens of dim 4096; latent 16x21x60x104 -> 32760
+    tokens), sequence-parallel over the ranks.  Random-init weights (seed 2),
+    N(0,1) latent and text, t = 500.  Device time with CUDA events per step,
+    L2 flushed between steps; the caller takes the max over ranks."""
+    from kairos_sensenova_b200.dit import DiTConfig, KairosDiT
+    cfg = DiTConfig()
+    model = KairosDiT(cfg, world=world, rank=rank)
+    gen = torch.Generator(device='cuda')
+    gen.manual_seed(2)
+    latent = torch.randn(cfg.in_dim, *cfg.latent, generator=gen, device='cuda')
+    ctx = torch.randn(cfg.text_len, cfg.text_dim, generator=gen, device='cuda')
+    ts = torch.tensor([500.0], device='cuda')
+    warm = max(3, args.warmup)
+    with torch.no_grad():
+        for _ in range(warm):
+            model(latent, ts, ctx)
+        sync_all()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(args.dit_steps)]
+        for s0, s1 in ev:
+            flush.zero_()
+            s0.record()
+            out = model(latent, ts, ctx)
+            s1.record()
+        sync_all()
+    ms = statistics.mean(s0.elapsed_time(s1) for s0, s1 in ev)
+    ok = bool(torch.isfinite(out.float()).all())
+    n = model.launches_per_step()
+    del model
+    torch.cuda.empty_cache()
+    return {'metric': 'DiT denoise-step ms', 'ms_per_step': ms, 'higher_is_better': False,
+            'steps': args.dit_steps, 'warmup': warm, 'n_gpus': world, 'finite_output': ok,
+            'gpu_launches': n * args.dit_steps,
+            'config': {'workload': 'config4 DiT step: 30 blocks, hidden 3072, 24x128 heads, FFN 8192 tanh-GELU, '
+                                   'GDN in 3 of 4 blocks + FP8 attention every 4th, cross-attn 512x4096, '
+                                   'latent 16x21x60x104 (32760 tokens), t=500',
+                       'parallelism': f'sequence/ulysses{world}', 'data': 'synthetic, random-init weights',
+                       'l2': 'flushed (256 MB write) between timed steps'}}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--gpus', type=int, default=1)
@@ -142,6 +189,8 @@ def main():
     ap.add_argument('--warmup', type=int, default=3)
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
     ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--dit-steps', type=int, default=3,
+                    help='timed DiT denoise steps (BASELINE config 4) after the hybrid block; 0 skips')
     args = ap.parse_args()
     world = int(os.environ.get('WORLD_SIZE', '1'))
     rank = int(os.environ.get('RANK', '0'))
@@ -185,6 +234,7 @@ def main():
             s1.record()
         sync_all()
         step_ms = statistics.mean(s0.elapsed_time(s1) for s0, s1, _, _ in ev)
+        launches = blk.launches_per_step()
         attn_ms = statistics.mean(a0.elapsed_time(a1) for _, _, a0, a1 in ev)
         # end to end through the public API with host buffers: every step copies its
         # input from pinned host memory and its result back; copies run on a side
@@ -226,10 +276,12 @@ def main():
         e2e_ms = e0.elapsed_time(e1) / args.steps
         clocks = sampler.stop() if sampler else None
 
-    t = torch.tensor([step_ms, attn_ms, e2e_ms], device='cuda')
+    del blk
+    dit = time_dit(args, world, rank, sync_all, flush) if args.dit_steps > 0 else None
+    t = torch.tensor([step_ms, attn_ms, e2e_ms, dit['ms_per_step'] if dit else 0.0], device='cuda')
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    step_ms, attn_ms, e2e_ms = t.tolist()
+    step_ms, attn_ms, e2e_ms, dit_ms = t.tolist()
     if rank == 0:
         bf16_tf, hbm, kind = _peaks()
         # QK^T (half the FLOPs) runs at the e4m3 rate, 2x bf16; P.V at the bf16 rate
@@ -250,7 +302,7 @@ def main():
                        'l2': 'flushed (256 MB write) between timed steps'},
             'e2e': {'value': T_FULL / (e2e_ms * 1e-3) / 1e6, 'unit': 'Mtokens/s',
                     'h2d_bytes_per_step': Tl * HIDDEN * 2, 'd2h_bytes_per_step': Tl * HIDDEN * 2},
-            'gpu_launches': blk.LAUNCHES_PER_STEP * args.steps,
+            'gpu_launches': launches * args.steps,
             'roofline': {'kernel': 'attention (e4m3 QK, bf16 PV)',
                          'bound': 'tensor', 'achieved': achieved,
                          'peak': fp8_peak, 'unit': 'TFLOP/s', 'frac': achieved / fp8_peak,
@@ -260,6 +312,9 @@ def main():
                          'peak_source': f'{kind} bf16 dense ({bf16_tf} TFLOP/s) x 4/3: QK at 2x (e4m3), PV at 1x (bf16)'},
             'clocks': clocks,
         }
+        if dit:
+            dit['ms_per_step'] = dit_ms
+            line['dit_step'] = dit
         if world == 1 and not args.no_cpu_baseline:
             ts = _cpu_sample_seconds(2)
             s = min(ts) * HEADS

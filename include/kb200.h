@@ -67,6 +67,11 @@ typedef struct KB200GdnArgs {
 
 /* Bytes of workspace kb200_gdn_chunk_fwd needs for these arguments. */
 size_t kb200_gdn_workspace_size(const KB200GdnArgs* a);
+
+/* Kernel launches kb200_gdn_chunk_fwd makes for these arguments (3, or 5 when the
+ * state pass is split into concurrent segments), -1 for invalid arguments.  A
+ * query for launch accounting; no counterpart in the reference. */
+int kb200_gdn_launch_count(const KB200GdnArgs* a);
 /* Launch the forward.  `workspace` must be 256-byte aligned. */
 int kb200_gdn_chunk_fwd(const KB200GdnArgs* a, void* workspace, size_t workspace_bytes,
                         void* stream);
@@ -97,7 +102,8 @@ int kb200_gdn_chunk_fwd_noalloc(const KB200GdnArgs* a, void* stream);
  *   base + (h / heads_per_block) * block_stride + row * ld + (h % heads_per_block) * head_dim + c % head_dim,
  * h = c / head_dim (heads_per_block = dim / head_dim for a plain [rows, ld] matrix),
  * so q/k can be normalised in place inside a destination-grouped projection.
- * x == y is allowed.
+ * x == y is allowed.  cos_sin == NULL skips the rotation (plain FusedRMSNorm, as
+ * CrossAttention.forward's norm_q / norm_k, kairos_dit.py:687-688).
  * --------------------------------------------------------------------- */
 int kb200_rmsnorm_rope(const void* x, void* y, int64_t rows, int64_t dim, int64_t head_dim, int64_t ld,
                        int64_t heads_per_block, int64_t block_stride, const float* weight,
@@ -174,6 +180,21 @@ int kb200_gdn_prologue(const KB200GdnPrologueArgs* a, void* stream);
 int kb200_rmsnorm_gated(const void* x, const void* gate, const float* weight, void* y,
                         int64_t rows, int64_t heads, int64_t D, int64_t ld_gate, float eps,
                         void* stream);
+
+/* ---------------------------------------------------------------------
+ * DiT norm sites: residual add, LayerNorm, modulation in one pass.
+ *   x <- bf16(x + gate * r)         when r != NULL (gate [dim] fp32, NULL = 1):
+ *                                   GateModule.forward / x.add_ (kairos_dit.py:700-701, 929-931, 968)
+ *   y  = bf16(LN(x) * m + a)        LayerNorm without affine, eps, then
+ *                                   m = mul_plus_one ? 1 + mul : mul (NULL: 1), a = add (NULL: 0):
+ *                                   modulate(norm(x), shift, scale) (kairos_dit.py:306-309, 873-874, 955-957),
+ *                                   the affine cross_attn_norm (mul = weight, add = bias, :797, 931)
+ *                                   and Head.forward (:1047-1052)
+ * x, y: [rows, dim] bf16 contiguous (y must not alias x); r: row stride ld_r.
+ * --------------------------------------------------------------------- */
+int kb200_residual_ln_mod(void* x, const void* r, int64_t rows, int64_t dim, int64_t ld_r,
+                          const float* gate, const float* mul, const float* add, int mul_plus_one,
+                          float eps, void* y, void* stream);
 
 #ifdef __cplusplus
 }

@@ -58,6 +58,7 @@ SIGNATURES = {
     'kb200_abi_version': (ctypes.c_int, []),
     'kb200_last_error': (ctypes.c_char_p, []),
     'kb200_gdn_workspace_size': (ctypes.c_size_t, [ctypes.POINTER(GdnArgs)]),
+    'kb200_gdn_launch_count': (ctypes.c_int, [ctypes.POINTER(GdnArgs)]),
     'kb200_gdn_chunk_fwd': (ctypes.c_int, [ctypes.POINTER(GdnArgs), ctypes.c_void_p,
                                            ctypes.c_size_t, ctypes.c_void_p]),
     'kb200_rmsnorm_rope': (ctypes.c_int, [ctypes.c_void_p] * 2 + [ctypes.c_int64] * 6 +
@@ -72,6 +73,8 @@ SIGNATURES = {
     'kb200_gdn_prologue': (ctypes.c_int, [ctypes.POINTER(GdnPrologueArgs), ctypes.c_void_p]),
     'kb200_rmsnorm_gated': (ctypes.c_int, [ctypes.c_void_p] * 4 + [ctypes.c_int64] * 4 +
                             [ctypes.c_float, ctypes.c_void_p]),
+    'kb200_residual_ln_mod': (ctypes.c_int, [ctypes.c_void_p] * 2 + [ctypes.c_int64] * 3 +
+                              [ctypes.c_void_p] * 3 + [ctypes.c_int, ctypes.c_float] + [ctypes.c_void_p] * 2),
 }
 
 

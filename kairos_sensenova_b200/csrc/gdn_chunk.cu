@@ -1085,6 +1085,12 @@ extern "C" size_t kb200_gdn_workspace_size(const KB200GdnArgs* a) {
   return ws_layout(a).total;
 }
 
+extern "C" int kb200_gdn_launch_count(const KB200GdnArgs* a) {
+  if (validate(a) != KB200_OK) return -1;
+  const StatePlan sp = state_plan(a);
+  return (a->num_chunks > 0 ? 2 : 0) + (sp.nseg > 1 ? 3 : 1);
+}
+
 extern "C" int kb200_gdn_chunk_fwd(const KB200GdnArgs* a, void* workspace, size_t workspace_bytes,
                                    void* stream) {
   if (int e = validate(a)) return e;

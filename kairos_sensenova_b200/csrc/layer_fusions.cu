@@ -246,8 +246,13 @@ __global__ void rmsnorm_rope_kernel(const __nv_bfloat16* x, __nv_bfloat16* y, in
     if (t >= rows) continue;
     const float rstd = 1.f / sqrtf(tot / dim + eps);
     const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw[q]);
-    const float* csr = cs + ((int64_t)t * (hd / 2) + cc / 2) * 2;
-    const float4 cs0 = *reinterpret_cast<const float4*>(csr), cs1 = *reinterpret_cast<const float4*>(csr + 4);
+    // no table: plain RMSNorm (identity rotation)
+    float4 cs0 = make_float4(1.f, 0.f, 1.f, 0.f), cs1 = cs0;
+    if (cs) {
+      const float* csr = cs + ((int64_t)t * (hd / 2) + cc / 2) * 2;
+      cs0 = *reinterpret_cast<const float4*>(csr);
+      cs1 = *reinterpret_cast<const float4*>(csr + 4);
+    }
     const float co[4] = {cs0.x, cs0.z, cs1.x, cs1.z}, si[4] = {cs0.y, cs0.w, cs1.y, cs1.w};
     uint4 outv;
     uint32_t* ov = reinterpret_cast<uint32_t*>(&outv);
@@ -258,6 +263,89 @@ __global__ void rmsnorm_rope_kernel(const __nv_bfloat16* x, __nv_bfloat16* y, in
       ov[j / 2] = pack_bf16(a * co[j / 2] - bb * si[j / 2], a * si[j / 2] + bb * co[j / 2]);
     }
     *reinterpret_cast<uint4*>(y + coff + (int64_t)t * ld) = outv;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Residual add + LayerNorm + modulation (the DiT block's norm sites,
+// kairos_dit.py:873-874, 929-933, 955-957 and Head.forward :1047-1052):
+//   x <- bf16(x + gate * r)                 (when r is given; gate NULL = 1)
+//   y  = bf16(LN(x) * m + a),  m = (mul_plus_one ? 1 + mul : mul)  (mul NULL: m = 1; add NULL: a = 0)
+// One CTA of dim/8 threads per RR rows; each thread holds 8 channels of a row in
+// registers; mean and variance by two block reductions (two-pass, fp32).
+// ---------------------------------------------------------------------------
+__global__ void residual_ln_mod_kernel(__nv_bfloat16* x, const __nv_bfloat16* r, int rows, int dim, int64_t ldr,
+                                       const float* __restrict__ gate, const float* __restrict__ mul,
+                                       const float* __restrict__ add, int plus_one, float eps,
+                                       __nv_bfloat16* y) {
+  __shared__ float red[2][RR][32];
+  const int c = threadIdx.x * 8, nw = (blockDim.x + 31) / 32, lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  float xv[RR][8];
+  float gv[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) gv[j] = gate ? gate[c + j] : 1.f;
+#pragma unroll
+  for (int q = 0; q < RR; ++q) {
+    const int t = blockIdx.x * RR + q;
+    uint4 raw = make_uint4(0, 0, 0, 0), rr = raw;
+    if (t < rows) {
+      raw = *reinterpret_cast<const uint4*>(x + (int64_t)t * dim + c);
+      if (r) rr = *reinterpret_cast<const uint4*>(r + (int64_t)t * ldr + c);
+    }
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
+    const __nv_bfloat16* er = reinterpret_cast<const __nv_bfloat16*>(&rr);
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float v = __bfloat162float(e[j]);
+      if (r) v = bf16_round(fmaf(gv[j], __bfloat162float(er[j]), v));
+      xv[q][j] = v;
+      s += v;
+    }
+    if (r && t < rows) {
+      uint4 o;
+      uint32_t* ov = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+      for (int j = 0; j < 8; j += 2) ov[j / 2] = pack_bf16(xv[q][j], xv[q][j + 1]);
+      *reinterpret_cast<uint4*>(x + (int64_t)t * dim + c) = o;
+    }
+    s = warp_sum(s);
+    if (lane == 0) red[0][q][wid] = s;
+  }
+  __syncthreads();
+  float mean[RR];
+#pragma unroll
+  for (int q = 0; q < RR; ++q) {
+    float tot = 0.f;
+    for (int i = 0; i < nw; ++i) tot += red[0][q][i];
+    mean[q] = tot / dim;
+    float s2 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) { const float d = xv[q][j] - mean[q]; s2 = fmaf(d, d, s2); }
+    s2 = warp_sum(s2);
+    if (lane == 0) red[1][q][wid] = s2;
+  }
+  __syncthreads();
+  float mv[8], av[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    mv[j] = mul ? (plus_one ? 1.f + mul[c + j] : mul[c + j]) : 1.f;
+    av[j] = add ? add[c + j] : 0.f;
+  }
+#pragma unroll
+  for (int q = 0; q < RR; ++q) {
+    const int t = blockIdx.x * RR + q;
+    if (t >= rows) continue;
+    float tot = 0.f;
+    for (int i = 0; i < nw; ++i) tot += red[1][q][i];
+    const float rstd = rsqrtf(tot / dim + eps);
+    uint4 o;
+    uint32_t* ov = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+    for (int j = 0; j < 8; j += 2)
+      ov[j / 2] = pack_bf16(fmaf((xv[q][j] - mean[q]) * rstd, mv[j], av[j]),
+                            fmaf((xv[q][j + 1] - mean[q]) * rstd, mv[j + 1], av[j + 1]));
+    *reinterpret_cast<uint4*>(y + (int64_t)t * dim + c) = o;
   }
 }
 
@@ -336,7 +424,7 @@ extern "C" int kb200_rmsnorm_gated(const void* x, const void* gate, const float*
 extern "C" int kb200_rmsnorm_rope(const void* x, void* y, int64_t rows, int64_t dim, int64_t head_dim,
                                   int64_t ld, int64_t heads_per_block, int64_t block_stride,
                                   const float* weight, const float* cos_sin, float eps, void* stream) {
-  if (!x || !y || !cos_sin) return set_error(KB200_ERR_INVALID, "rmsnorm_rope: null pointer");
+  if (!x || !y) return set_error(KB200_ERR_INVALID, "rmsnorm_rope: null pointer");
   if (rows < 0 || dim <= 0 || dim % 8 || dim / 8 > 1024 || head_dim <= 0 || head_dim % 8 ||
       dim % head_dim || heads_per_block <= 0)
     return set_error(KB200_ERR_INVALID, "rmsnorm_rope: need dim %% 8 == 0, dim <= 8192, head_dim | dim");
@@ -348,4 +436,21 @@ extern "C" int kb200_rmsnorm_rope(const void* x, void* y, int64_t rows, int64_t 
       (const __nv_bfloat16*)x, (__nv_bfloat16*)y, (int)rows, (int)dim, (int)head_dim, ld, (int)heads_per_block,
       block_stride, weight, cos_sin, eps);
   return check_launch("rmsnorm_rope_kernel");
+}
+
+extern "C" int kb200_residual_ln_mod(void* x, const void* r, int64_t rows, int64_t dim, int64_t ld_r,
+                                     const float* gate, const float* mul, const float* add, int mul_plus_one,
+                                     float eps, void* y, void* stream) {
+  if (!x || !y) return set_error(KB200_ERR_INVALID, "residual_ln_mod: null pointer");
+  if (rows < 0 || dim <= 0 || dim % 8 || dim / 8 > 1024)
+    return set_error(KB200_ERR_INVALID, "residual_ln_mod: need dim %% 8 == 0 and dim <= 8192");
+  if (!aligned16(x) || !aligned16(y) || (r && (!aligned16(r) || ld_r % 8 || ld_r < dim)))
+    return set_error(KB200_ERR_ALIGN, "residual_ln_mod: rows must be 16-byte aligned");
+  if (x == y) return set_error(KB200_ERR_INVALID, "residual_ln_mod: y must not alias x");
+  if (rows == 0) return KB200_OK;
+  fuse::residual_ln_mod_kernel<<<(unsigned)((rows + fuse::RR - 1) / fuse::RR), (unsigned)(dim / 8), 0,
+                                 static_cast<cudaStream_t>(stream)>>>(
+      (__nv_bfloat16*)x, (const __nv_bfloat16*)r, (int)rows, (int)dim, r ? ld_r : dim, gate, mul, add,
+      mul_plus_one, eps, (__nv_bfloat16*)y);
+  return check_launch("residual_ln_mod_kernel");
 }

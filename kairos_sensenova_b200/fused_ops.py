@@ -5,6 +5,9 @@
   in one launch.
 * :func:`rms_norm_gated` -- ``FusedRMSNormGated`` (swish gate) forward
   (``fla/modules/fused_norm_gate.py:1024-1085``).
+* :func:`rmsnorm_rope` -- the attention prologue: full-dim RMSNorm (+ 3-D RoPE).
+* :func:`residual_ln_mod` -- the DiT block's residual add + LayerNorm +
+  modulation sites (``kairos_dit.py:306-309, 873-874, 929-957``).
 """
 from __future__ import annotations
 
@@ -117,7 +120,7 @@ def rmsnorm_rope(x: torch.Tensor, weight, cos_sin: torch.Tensor, head_dim: int, 
     ``kairos_dit.py:452-456``).  ``x``: [..., dim] bf16 (rows = all leading
     elements) or, with ``rows/dim/ld/heads_per_block/block_stride``, a
     destination-grouped projection view; ``out`` defaults to a new tensor
-    (pass ``out=x`` to work in place)."""
+    (pass ``out=x`` to work in place).  ``cos_sin=None``: plain RMSNorm."""
     dev = x.device
     if dev.type != 'cuda':
         raise RuntimeError('rmsnorm_rope: CUDA tensors required (no CPU path)')
@@ -131,13 +134,44 @@ def rmsnorm_rope(x: torch.Tensor, weight, cos_sin: torch.Tensor, head_dim: int, 
     if out is None:
         out = torch.empty_like(x)
     w = None if weight is None else weight.to(dev, torch.float32).contiguous()
-    cs = cos_sin.to(dev, torch.float32).contiguous()
-    if cs.numel() < rows * head_dim:
+    cs = None if cos_sin is None else cos_sin.to(dev, torch.float32).contiguous()
+    if cs is not None and cs.numel() < rows * head_dim:
         raise ValueError('rmsnorm_rope: cos/sin table smaller than rows x head_dim/2 x 2')
     with torch.cuda.device(dev):
         _lib.check(_lib.lib().kb200_rmsnorm_rope(x.data_ptr(), out.data_ptr(), rows, dim, head_dim, ld,
                                                   heads_per_block, block_stride,
-                                                  None if w is None else w.data_ptr(), cs.data_ptr(),
+                                                  None if w is None else w.data_ptr(),
+                                                  None if cs is None else cs.data_ptr(),
                                                   float(eps), _stream(dev)),
                    'rmsnorm_rope')
+    return out
+
+
+def _vec(t, dev):
+    return None if t is None else t.to(device=dev, dtype=torch.float32).contiguous()
+
+
+def residual_ln_mod(x: torch.Tensor, r, gate, mul, add, mul_plus_one: bool = True, eps: float = 1e-6,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+    """``x <- x + gate * r`` in place (when ``r`` is given; ``gate`` None = 1), then
+    ``out = LN(x) * m + add`` with ``m = 1 + mul`` (``mul_plus_one``) or ``mul``
+    (None: 1; ``add`` None: 0).  x: [rows, dim] bf16 contiguous; r: [rows, dim]
+    bf16 rows with unit column stride; gate/mul/add: [dim] vectors."""
+    dev = x.device
+    if dev.type != 'cuda':
+        raise RuntimeError('residual_ln_mod: CUDA tensors required (no CPU path)')
+    if x.dtype != torch.bfloat16 or not x.is_contiguous() or x.dim() != 2:
+        raise ValueError('residual_ln_mod: x must be a contiguous 2-D bf16 tensor (updated in place)')
+    rows, dim = x.shape
+    ldr = 0
+    if r is not None:
+        r, ldr = _rows(r, dim)
+    if out is None:
+        out = torch.empty_like(x)
+    g, m, a = _vec(gate, dev), _vec(mul, dev), _vec(add, dev)
+    p = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+    with torch.cuda.device(dev):
+        _lib.check(_lib.lib().kb200_residual_ln_mod(x.data_ptr(), p(r), rows, dim, ldr, p(g), p(m), p(a),
+                                                     int(bool(mul_plus_one)), float(eps), out.data_ptr(),
+                                                     _stream(dev)), 'residual_ln_mod')
     return out

@@ -1,41 +1,19 @@
-"""The sequence-parallel hybrid block of the benchmark (one GDN mixer chain
-and one FP8-attention mixer chain), Ulysses-sharded over P ranks.
+"""The sequence-parallel hybrid block of the benchmark: one
+GDN mixer chain and one FP8-attention mixer chain, Ulysses-sharded over P
+ranks (the chains themselves are :mod:`.mixers`).
 
 Per rank the input is a sequence shard ``x_local [T/P, hidden]`` (bf16).
-
-GDN chain (the GDN half of ``DiTBlock.forward``, ``kairos_dit.py:858-928``,
-re-partitioned Ulysses-style instead of the reference's per-owner broadcast):
-  1. one batched projection GEMM writes q|k|v|a|b already grouped by
-     destination rank: ``[P, T/P, C_loc]`` (cuBLAS);
-  2. ``all_to_all_single`` seq->head: every rank gets all T tokens of its
-     ``H/P`` heads (NCCL over NVLink);
-  3. prologue kernel: short convs + SiLU, beta, g (the causal conv needs the
-     full sequence of a head, which the rank now holds -- no halo exchange);
-  4. chunked GDN kernels;
-  5. ``all_to_all_single`` head->seq;
-  6. epilogue kernel: gated RMSNorm with ``g_proj(x_local)`` (seq-sharded, so
-     the gate never crosses the wire), then ``o_proj``.
-
-Attention chain (``SelfAttentionTP.forward``, ``kairos_dit.py:603-650``):
-  q|k|v projection grouped by destination, seq->head all-to-all, FP8
-  attention on the rank's heads, head->seq all-to-all, ``o`` projection.
-  q and k get the layer's full-dimension RMSNorm and 3-D RoPE in place in the
-  projection buffer before the exchange (one fused kernel, ``kairos_dit.py:452-456``).
+Weights are drawn on the device from a seeded generator, identically on every
+rank; the full-size copies stay on the block so that tests can hand them to
+the CPU oracle.
 """
 from __future__ import annotations
 
 import math
 
 import torch
-import torch.distributed as dist
 
-from .attention import attention_fp8
-from .fused_ops import freqs_cis_3d, gdn_prologue, rms_norm_gated, rmsnorm_rope, rope_table
-from .gated_delta_rule import chunk_gated_delta_rule
-
-
-def _round8(n):
-    return (n + 7) // 8 * 8
+from .mixers import AttnMixer, GdnMixer
 
 
 class HybridBlock:
@@ -70,90 +48,18 @@ class HybridBlock:
         # attention q/k RMSNorm weights (FusedRMSNorm init: ones) and the 3-D RoPE grid
         self.nq = torch.ones(HD, device=device)
         self.nk = torch.ones(HD, device=device)
-        self.grid, self.attn_eps, self._rope = grid, attn_eps, None
-        self._pack()
+        self.grid, self.attn_eps = grid, attn_eps
+        self.gdn = GdnMixer(self.Wq, self.Wk, self.Wv, self.Wa, self.Wb, self.Wg, self.Wo, self.cq, self.ck,
+                            self.cv, self.A_log, self.dt_bias, self.o_norm_w, heads, head_dim, world, rank,
+                            group, norm_eps)
+        self.attn = AttnMixer(self.Aq, self.Ak, self.Av, self.Ao, self.nq, self.nk, heads, head_dim, world,
+                              rank, group, attn_eps, grid=grid)
 
-    # ------------------------------------------------------------------ layout
-    def _pack(self):
-        """Group projection columns by destination rank (the all-to-all send order)."""
-        P, Hl, D = self.P, self.Hl, self.D
-        rows = lambda W, r, d: W[r * Hl * d:(r + 1) * Hl * d]  # noqa: E731
-        self.C_gdn = _round8(3 * Hl * D + 2 * Hl)
-        self.C_attn = 3 * Hl * D
-        Wg, Wa = [], []
-        for r in range(P):
-            blk = torch.cat([rows(self.Wq, r, D), rows(self.Wk, r, D), rows(self.Wv, r, D),
-                             rows(self.Wa, r, 1), rows(self.Wb, r, 1)])
-            pad = self.C_gdn - blk.shape[0]
-            if pad:
-                blk = torch.cat([blk, blk.new_zeros(pad, blk.shape[1])])
-            Wg.append(blk.t())
-            Wa.append(torch.cat([rows(self.Aq, r, D), rows(self.Ak, r, D), rows(self.Av, r, D)]).t())
-        self.W_gdn = torch.stack(Wg).contiguous()      # [P, hidden, C_gdn]
-        self.W_attn = torch.stack(Wa).contiguous()     # [P, hidden, C_attn]
-        sl = slice(self.rank * Hl * D, (self.rank + 1) * Hl * D)
-        self.cq_l, self.ck_l, self.cv_l = self.cq[sl], self.ck[sl], self.cv[sl]
-        hs = slice(self.rank * Hl, (self.rank + 1) * Hl)
-        self.A_log_l, self.dt_bias_l = self.A_log[hs], self.dt_bias[hs]
-        self.WgT = self.Wg.t().contiguous()
-        self.WoT = self.Wo.t().contiguous()
-        self.AoT = self.Ao.t().contiguous()
-
-    def _a2a(self, send):
-        if self.P == 1:
-            return send
-        recv = torch.empty_like(send)
-        dist.all_to_all_single(recv, send, group=self.group)
-        return recv
-
-    def _head_to_seq(self, o_heads, Tl):
-        """[T, Hl*D] head-sharded -> [Tl, H*D] sequence-sharded."""
-        send = o_heads.reshape(self.P, Tl, self.Hl * self.D)
-        recv = self._a2a(send)
-        return recv.permute(1, 0, 2).reshape(Tl, self.H * self.D) if self.P > 1 else recv.reshape(Tl, -1)
-
-    # ------------------------------------------------------------------ chains
     def gdn_chain(self, x_local):
-        Tl = x_local.shape[0]
-        T = Tl * self.P
-        Hl, D = self.Hl, self.D
-        send = torch.matmul(x_local.unsqueeze(0), self.W_gdn)          # [P, Tl, C_gdn]
-        recv = self._a2a(send).reshape(T, self.C_gdn)
-        c = lambda i: recv[:, i * Hl * D:(i + 1) * Hl * D]  # noqa: E731
-        ab = 3 * Hl * D
-        q, k, v, g, beta = gdn_prologue(c(0), c(1), c(2), recv[:, ab:ab + Hl], recv[:, ab + Hl:ab + 2 * Hl],
-                                        self.cq_l, self.ck_l, self.cv_l, self.A_log_l, self.dt_bias_l,
-                                        Hl, 1, T)
-        o, _ = chunk_gated_delta_rule(q, k, v, g, beta, use_qk_l2norm_in_kernel=True)
-        o_seq = self._head_to_seq(o.reshape(T, Hl * D), Tl)
-        gate = x_local @ self.WgT
-        y = rms_norm_gated(o_seq.reshape(Tl, self.H, D), gate.reshape(Tl, self.H, D), self.o_norm_w, self.eps)
-        return y.reshape(Tl, -1) @ self.WoT
-
-    def rope(self, T):
-        """(cos, sin) table [T, D/2, 2] of the 3-D RoPE grid (a 1-D frame axis when
-        the grid does not hold T tokens)."""
-        if self._rope is None or self._rope.shape[0] != T:
-            f, h, w = self.grid if self.grid[0] * self.grid[1] * self.grid[2] == T else (T, 1, 1)
-            self._rope = rope_table(freqs_cis_3d(self.D, f, h, w), self.W_attn.device)
-        return self._rope
+        return self.gdn(x_local)
 
     def attn_chain(self, x_local, events=None):
-        Tl = x_local.shape[0]
-        T = Tl * self.P
-        Hl, D = self.Hl, self.D
-        send = torch.matmul(x_local.unsqueeze(0), self.W_attn)          # [P, Tl, 3*Hl*D]
-        # q/k RMSNorm over all heads + RoPE, in place, sequence-sharded (before the exchange)
-        cs = self.rope(T)[self.rank * Tl:(self.rank + 1) * Tl]
-        for col, wgt in ((0, self.nq), (Hl * D, self.nk)):
-            view = send[..., col:]
-            rmsnorm_rope(view, wgt, cs, D, eps=self.attn_eps, out=view, rows=Tl, dim=self.H * D,
-                         ld=self.C_attn, heads_per_block=Hl, block_stride=Tl * self.C_attn)
-        recv = self._a2a(send).reshape(T, self.C_attn)
-        q, k, v = (recv[:, i * Hl * D:(i + 1) * Hl * D].reshape(1, T, Hl * D) for i in range(3))
-        o = attention_fp8(q, k, v, Hl, events=events)
-        o_seq = self._head_to_seq(o.reshape(T, Hl * D), Tl)
-        return o_seq @ self.AoT
+        return self.attn(x_local, events)
 
     def forward(self, x_local, events=None):
         """One hybrid step: the GDN chain, then the attention chain on its output.
@@ -161,6 +67,6 @@ class HybridBlock:
         y = self.gdn_chain(x_local)
         return self.attn_chain(y, events)
 
-    # kernel launches of this library per forward(): prologue, 3 GDN kernels,
-    # gated RMSNorm; q and k RMSNorm+RoPE, amax, quantise, attention
-    LAUNCHES_PER_STEP = 10
+    def launches_per_step(self):
+        """Kernel launches of this library per forward() (as of the last call)."""
+        return self.gdn.launches + self.attn.launches

@@ -1,0 +1,107 @@
+"""CPU restatement of the Kairos DiT denoise step (test infrastructure only).
+
+``KairosDiT.forward`` (``kairos/modules/dits/kairos_dit.py:1187-1266``) with
+``DiTBlock.forward`` (``:823-972``) in fp32 on the host, for the weights dict of
+``kairos_sensenova_b200.dit.make_weights`` and a ``DiTConfig``:
+
+* time / text embeddings (``:1101-1113, 1191-1194``; sinusoid ``common.py:4-13``);
+* patch embedding as the Conv3d it is (``:1097, 1167-1174``);
+* per block: LayerNorm + modulate (``:306-309, 873-874``), the mixer
+  (GatedDeltaNet chain / attention chain, :mod:`oracle.hybrid` and
+  ``SelfAttention.forward`` ``:452-479`` with biases), gated residual
+  (``:696-701, 929``), cross-attention (``CrossAttention.forward`` ``:681-694``)
+  after the affine ``cross_attn_norm``, FFN with its modulation and gate
+  (``:950-970``);
+* head (``Head.forward`` ``:1047-1052``) and unpatchify (``:1176-1181``).
+
+Only the model pieces are restated here; the GDN and attention arithmetic
+comes from :mod:`oracle.gdn` (pinned to the reference's golden vectors) and
+torch's SDPA (the reference's own fallback).
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+
+from .hybrid import freqs_cis_3d, gdn_chain
+from .layers import rmsnorm_rope
+
+
+def _f(t):
+    return t.detach().float().cpu()
+
+
+def _ln(x, eps):
+    return F.layer_norm(x, x.shape[-1:], eps=eps)
+
+
+def _rms(x, w, eps):
+    return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * w
+
+
+def _sdpa(q, k, v, H):
+    Tq, Tk, D = q.shape[0], k.shape[0], q.shape[1] // H
+    o = F.scaled_dot_product_attention(q.reshape(1, Tq, H, D).transpose(1, 2), k.reshape(1, Tk, H, D).transpose(1, 2),
+                                       v.reshape(1, Tk, H, D).transpose(1, 2))
+    return o.transpose(1, 2).reshape(Tq, H * D)
+
+
+def self_attention(b, x, H, D, grid, eps):
+    """``SelfAttention.forward`` (``kairos_dit.py:452-479``), full attention."""
+    T = x.shape[0]
+    fr = freqs_cis_3d(D, *grid)
+    q = rmsnorm_rope((x @ b['Aq'].t() + b['Abq'])[None], b['nq'], fr, H, eps)[0].float()
+    k = rmsnorm_rope((x @ b['Ak'].t() + b['Abk'])[None], b['nk'], fr, H, eps)[0].float()
+    v = x @ b['Av'].t() + b['Abv']
+    return _sdpa(q, k, v, H) @ b['Ao'].t() + b['Abo']
+
+
+def cross_attention(b, y, ctx, H, eps):
+    q = _rms(y @ b['Cq'].t() + b['Cbq'], b['Cnq'], eps)
+    k = _rms(ctx @ b['Ck'].t() + b['Cbk'], b['Cnk'], eps)
+    v = ctx @ b['Cv'].t() + b['Cbv']
+    return _sdpa(q, k, v, H) @ b['Co'].t() + b['Cbo']
+
+
+def dit_forward(weights, cfg, latent, timestep, context):
+    """latent [in_dim, F, H, W], timestep [1], context [text_len, text_dim] -> [out_dim, F, H, W] fp32."""
+    w = {k: _f(v) for k, v in weights.items() if k != 'blocks'}
+    D, H, hd, eps = cfg.dim, cfg.heads, cfg.head_dim, cfg.eps
+    half = cfg.freq_dim // 2
+    pos = timestep.double().cpu().reshape(-1)
+    s = torch.outer(pos, torch.pow(10000, -torch.arange(half, dtype=torch.float64).div(half)))
+    t_in = torch.cat([torch.cos(s), torch.sin(s)], 1).float()
+    t = F.silu(t_in @ w['time_w1'].t() + w['time_b1']) @ w['time_w2'].t() + w['time_b2']
+    t_mod = (F.silu(t) @ w['tproj_w'].t() + w['tproj_b']).reshape(6, D)
+    ctx = _f(context)
+    ctx = F.silu(ctx @ w['text_w1'].t() + w['text_b1']) @ w['text_w2'].t() + w['text_b2']
+    pf, ph, pw = cfg.patch
+    conv_w = w['patch_w'].reshape(D, cfg.in_dim, pf, ph, pw)
+    x = F.conv3d(_f(latent)[None], conv_w, w['patch_b'], stride=cfg.patch)[0]      # [D, f, h, w]
+    grid = x.shape[1:]
+    x = x.flatten(1).t()                                                             # [T, D]
+    for i, braw in enumerate(weights['blocks']):
+        b = {k: _f(v) for k, v in braw.items()}
+        m = b['mod'] + t_mod
+        y = _ln(x, eps) * (1 + m[0]) + m[1]
+        if cfg.is_gdn(i):
+            mix = gdn_chain(b, y, H, hd, eps)
+        else:
+            mix = self_attention(b, y, H, hd, tuple(grid), eps)
+        x = x + m[2] * mix
+        x = x + cross_attention(b, _ln(x, eps) * b['ca_w'] + b['ca_b'], ctx, H, eps)
+        y = _ln(x, eps) * (1 + m[3]) + m[4]
+        h = y @ b['W1'].t() + b['b1']
+        h = F.gelu(h, approximate='tanh') if cfg.ffn_act == 'gelu_tanh' else F.silu(h)
+        x = x + m[5] * (h @ b['W2'].t() + b['b2'])
+    shift, scale = w['head_mod'] + t
+    out = (_ln(x, eps) * (1 + scale) + shift) @ w['head_w'].t() + w['head_b']        # [T, pf ph pw c]
+    f_, h_, w_ = grid
+    c = cfg.out_dim
+    return out.reshape(f_, h_, w_, pf, ph, pw, c).permute(6, 0, 3, 1, 4, 2, 5).reshape(c, f_ * pf, h_ * ph, w_ * pw)
+
+
+def tokens_of(cfg):
+    return math.prod(cfg.grid)
