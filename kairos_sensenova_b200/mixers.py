@@ -28,6 +28,8 @@ full-size ones after construction.
 """
 from __future__ import annotations
 
+import contextlib
+
 import torch
 import torch.distributed as dist
 
@@ -40,12 +42,76 @@ def _round8(n):
     return (n + 7) // 8 * 8
 
 
+_COMM_STREAMS = {}
+
+
+def _comm_stream(dev):
+    s = _COMM_STREAMS.get(dev)
+    if s is None:
+        s = _COMM_STREAMS[dev] = torch.cuda.Stream(dev)
+    return s
+
+
 class _Ulysses:
+    # token slabs of the seq->head exchange: the projection GEMM of slab i+1 runs
+    # while slab i crosses NVLink (0 = choose from the shard size)
+    slabs = 0
+
     def __init__(self, heads, head_dim, world, rank, group):
         if heads % world:
             raise ValueError('heads must divide evenly over ranks')
         self.H, self.D, self.P, self.rank, self.group = heads, head_dim, world, rank, group
         self.Hl = heads // world
+
+    def _project_exchange(self, x_local, W, b, post=None):
+        """Projection grouped by destination + seq->head exchange: returns
+        ``[T, C]`` (all tokens of this rank's heads, in token order).
+
+        With P > 1 the rows of the shard are processed in slabs: the GEMM of
+        a slab writes ``[P, n, C]`` (destination-major, so each destination's
+        part is contiguous), ``post`` (if given) transforms it in place, and
+        grouped NCCL sends/receives on a side stream move it while the next
+        slab is projected.  Rank ``src``'s rows ``[r0, r0+n)`` land in rows
+        ``src * T/P + r0 ..`` of the result, which is therefore already in
+        global token order."""
+        Tl = x_local.shape[0]
+        C = W.shape[-1]
+        if self.P == 1:
+            send = self._project(x_local, W, b)
+            if post is not None:
+                post(send, 0)
+            return send.reshape(Tl, C)
+        P, rank = self.P, self.rank
+        ns = self.slabs or max(1, min(4, Tl // 1024))
+        step = -(-Tl // ns)
+        recv = torch.empty(P, Tl, C, device=x_local.device, dtype=x_local.dtype)
+        cuda = x_local.is_cuda          # (CPU tensors: the gloo tests of the data layout)
+        comp = torch.cuda.current_stream(x_local.device) if cuda else None
+        comm = _comm_stream(x_local.device) if cuda else None
+        for r0 in range(0, Tl, step):
+            r1 = min(Tl, r0 + step)
+            send = self._project(x_local[r0:r1], W, b)                 # [P, n, C]
+            if post is not None:
+                post(send, r0)
+            if cuda:
+                comm.wait_stream(comp)
+            with torch.cuda.stream(comm) if cuda else contextlib.nullcontext():
+                ops = []
+                for peer in range(P):
+                    if peer != rank:
+                        ops.append(dist.P2POp(dist.isend, send[peer], self._global(peer), self.group))
+                        ops.append(dist.P2POp(dist.irecv, recv[peer, r0:r1], self._global(peer), self.group))
+                for req in dist.batch_isend_irecv(ops):
+                    req.wait()
+                recv[rank, r0:r1].copy_(send[rank])
+            if cuda:
+                send.record_stream(comm)
+        if cuda:
+            comp.wait_stream(comm)
+        return recv.reshape(P * Tl, C)
+
+    def _global(self, peer):
+        return peer if self.group is None else dist.get_global_rank(self.group, peer)
 
     def _rows(self, W, r, d):
         return W[r * self.Hl * d:(r + 1) * self.Hl * d]
@@ -105,8 +171,7 @@ class GdnMixer(_Ulysses):
         Tl = x_local.shape[0]
         T = Tl * self.P
         Hl, D = self.Hl, self.D
-        send = self._project(x_local, self.W, None)                     # [P, Tl, C]
-        recv = self._a2a(send).reshape(T, self.C)
+        recv = self._project_exchange(x_local, self.W, None)            # [T, C]
         c = lambda i: recv[:, i * Hl * D:(i + 1) * Hl * D]  # noqa: E731
         ab = 3 * Hl * D
         q, k, v, g, beta = gdn_prologue(c(0), c(1), c(2), recv[:, ab:ab + Hl], recv[:, ab + Hl:ab + 2 * Hl],
@@ -124,7 +189,7 @@ class AttnMixer(_Ulysses):
     full-dimension RMSNorm weights; ``grid``: the (frames, height, width) latent
     grid of the 3-D RoPE (a 1-D axis when it does not hold T tokens)."""
 
-    # q and k RMSNorm+RoPE, amax, quantise, attention
+    # q and k RMSNorm+RoPE per exchange slab, amax, quantise, attention (updated by each call)
     launches = 5
 
     def __init__(self, Wq, Wk, Wv, Wo, nq, nk, heads, head_dim, world=1, rank=0, group=None, eps=1e-6,
@@ -156,14 +221,20 @@ class AttnMixer(_Ulysses):
         Tl = x_local.shape[0]
         T = Tl * self.P
         Hl, D = self.Hl, self.D
-        send = self._project(x_local, self.W, self.b)                   # [P, Tl, 3*Hl*D]
-        # q/k RMSNorm over all heads + RoPE, in place, sequence-sharded (before the exchange)
         cs = self.rope(T)[self.rank * Tl:(self.rank + 1) * Tl]
-        for col, wgt in ((0, self.nq), (Hl * D, self.nk)):
-            view = send[..., col:]
-            rmsnorm_rope(view, wgt, cs, D, eps=self.eps, out=view, rows=Tl, dim=self.H * D,
-                         ld=self.C, heads_per_block=Hl, block_stride=Tl * self.C)
-        recv = self._a2a(send).reshape(T, self.C)
+
+        self.launches = 3
+
+        def norm_rope(send, r0):
+            # q/k RMSNorm over all heads + RoPE, in place, sequence-sharded (before the exchange)
+            self.launches += 2
+            n = send.shape[1]
+            for col, wgt in ((0, self.nq), (Hl * D, self.nk)):
+                view = send[..., col:]
+                rmsnorm_rope(view, wgt, cs[r0:r0 + n], D, eps=self.eps, out=view, rows=n, dim=self.H * D,
+                             ld=self.C, heads_per_block=Hl, block_stride=n * self.C)
+
+        recv = self._project_exchange(x_local, self.W, self.b, norm_rope)  # [T, 3*Hl*D]
         q, k, v = (recv[:, i * Hl * D:(i + 1) * Hl * D].reshape(1, T, Hl * D) for i in range(3))
         o = attention_fp8(q, k, v, Hl, events=events)
         o_seq = self._head_to_seq(o.reshape(T, Hl * D), Tl)

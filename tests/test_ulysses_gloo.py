@@ -1,5 +1,6 @@
 """Ulysses all-to-all wrapper on CPU gloo ranks (world 2 and 3), checked
-against the index arithmetic of the reference's semantics (oracle.layers)."""
+against the index arithmetic of the reference's semantics (oracle.layers),
+and the mixers' slabbed projection exchange against a plain product."""
 import os
 import socket
 
@@ -53,6 +54,28 @@ def _worker(rank, world, port, q):
             all2all_head_to_seq(torch.zeros(1, world + 1, 4), None)
         with pytest.raises(RuntimeError):
             all2all_seq_to_head(xu, None, tp_chunk_list=chunks, head_dim=None)
+        # slabbed projection + seq->head exchange of the mixers (destination-grouped
+        # GEMM per token slab, grouped sends/receives): rank r ends up with
+        # x_full @ W[r] (+ b[r]) in global token order; `post` sees each slab
+        from kairos_sensenova_b200.mixers import _Ulysses
+        T, hid, C = 12 * world, 8, 5
+        xf = torch.randn(T, hid, generator=g)
+        W = torch.randn(world, hid, C, generator=g)
+        b = torch.randn(world, C, generator=g)
+        Tl = T // world
+        u = _Ulysses(2 * world, 4, world, rank, None)
+        u.slabs = 3
+        seen = []
+
+        def post(send, r0):
+            seen.append((r0, send.shape[1]))
+            send[..., 0] = send[..., 0] + (rank * Tl + r0 + torch.arange(send.shape[1])).float()
+
+        got = u._project_exchange(xf[rank * Tl:(rank + 1) * Tl].clone(), W, b, post)
+        want = xf @ W[rank] + b[rank]
+        want[:, 0] += torch.arange(T).float()
+        assert got.shape == (T, C) and torch.allclose(got, want, atol=1e-5), (got - want).abs().max()
+        assert seen == [(0, 4), (4, 4), (8, 4)]
         dist.barrier()
         q.put((rank, 'ok'))
     except Exception as e:  # pragma: no cover - reported to the parent
