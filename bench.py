@@ -176,22 +176,26 @@ def time_dit(args, world, rank, sync_all, flush):
     ctx = torch.randn(cfg.text_len, cfg.text_dim, generator=gen, device='cuda')
     ts = torch.tensor([500.0], device='cuda')
     warm = max(3, args.warmup)
+    step = model
+    if not args.eager_dit:
+        from kairos_sensenova_b200.graphs import GraphedStep
+        step = GraphedStep(model, latent, ts, ctx)
     with torch.no_grad():
         for _ in range(warm):
-            model(latent, ts, ctx)
+            step(latent, ts, ctx)
         sync_all()
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
               for _ in range(args.dit_steps)]
         for s0, s1 in ev:
             flush.zero_()
             s0.record()
-            out = model(latent, ts, ctx)
+            out = step(latent, ts, ctx)
             s1.record()
         sync_all()
     ms = statistics.mean(s0.elapsed_time(s1) for s0, s1 in ev)
     ok = bool(torch.isfinite(out.float()).all())
     n = model.launches_per_step()
-    del model
+    del model, step
     torch.cuda.empty_cache()
     return {'metric': 'DiT denoise-step ms', 'ms_per_step': ms, 'higher_is_better': False,
             'steps': args.dit_steps, 'warmup': warm, 'n_gpus': world, 'finite_output': ok,
@@ -200,6 +204,7 @@ def time_dit(args, world, rank, sync_all, flush):
                                    'GDN in 3 of 4 blocks + FP8 attention every 4th, cross-attn 512x4096, '
                                    'latent 16x21x60x104 (32760 tokens), t=500',
                        'parallelism': f'sequence/ulysses{world}', 'data': 'synthetic, random-init weights',
+                       'launch': 'eager' if args.eager_dit else 'one CUDA graph per step',
                        'l2': 'flushed (256 MB write) between timed steps'}}
 
 
@@ -210,6 +215,8 @@ def main():
     ap.add_argument('--warmup', type=int, default=3)
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
     ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--eager-dit', action='store_true',
+                    help='time the DiT step issued op by op instead of as one captured CUDA graph')
     ap.add_argument('--dit-steps', type=int, default=3,
                     help='timed DiT denoise steps (BASELINE config 4) after the hybrid block; 0 skips')
     args = ap.parse_args()

@@ -57,3 +57,23 @@ def test_dit_step_small_vs_oracle(pattern):
     ref = dit_forward(w, cfg, latent, t, ctx)
     assert _cos(out, ref) >= 0.999
     assert max_rel(out, ref) <= 3e-2
+
+
+def test_dit_step_cuda_graph_replays_eager_results():
+    """The captured step (persistent buffers, one graph launch) gives the eager
+    step's output bit for bit, for two different inputs in a row."""
+    from kairos_sensenova_b200.dit import DiTConfig, KairosDiT, make_weights
+    from kairos_sensenova_b200.graphs import GraphedStep
+    cfg = DiTConfig(dim=256, heads=2, ffn_dim=512, layers=4, text_dim=64, text_len=16, latent=(4, 16, 16))
+    model = KairosDiT(cfg, weights=make_weights(cfg, 'cuda', seed=2))
+    gen = torch.Generator(device='cuda').manual_seed(9)
+    ins = [(torch.randn(cfg.in_dim, *cfg.latent, generator=gen, device='cuda'),
+            torch.tensor([t], device='cuda'),
+            torch.randn(cfg.text_len, cfg.text_dim, generator=gen, device='cuda')) for t in (500.0, 250.0)]
+    with torch.no_grad():
+        eager = [model(*x).clone() for x in ins]
+        step = GraphedStep(model, *ins[0])
+        for x, e in zip(ins, eager):
+            out = step(*x)
+            torch.cuda.synchronize()
+            assert torch.equal(out, e)

@@ -1,6 +1,8 @@
 """Sequence-parallel paths on 2 GPUs (NCCL, one process per GPU): the hybrid
 block and a small DiT step sharded over two ranks must match the same model
-run on one GPU.  Skipped on boxes with fewer than two GPUs.
+run on one GPU, and the DiT step captured as one CUDA graph (NCCL sends and
+receives inside) must match its eager run.  Skipped on boxes with fewer than
+two GPUs.
 
 Tolerances: the sharded run changes only the GEMM shapes, the per-rank head
 split of the GDN state pass (V-slice width, segment count) and the order of
@@ -58,6 +60,11 @@ def _worker(rank, world, port, q):
             o1 = KairosDiT(cfg, weights=w)(lat, t, ctx)
             o2 = KairosDiT(cfg, world=world, rank=rank, weights=w)(lat, t, ctx)
             res['dit'] = _cmp(o2, o1)
+            from kairos_sensenova_b200.graphs import GraphedStep
+            m2 = KairosDiT(cfg, world=world, rank=rank, weights=w)
+            o3 = GraphedStep(m2, lat, t, ctx)(lat, t, ctx)
+            torch.cuda.synchronize()
+            res['dit_graph'] = _cmp(o3, o2)
         dist.barrier()
         q.put((rank, res))
     except Exception as e:  # pragma: no cover - reported to the parent
