@@ -16,6 +16,8 @@ KB_DEVI uint32_t pack_bf16(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&t);
 }
 KB_DEVI float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+// The two bf16 of a pack_bf16 word as floats (low half first).
+KB_DEVI float2 unpack_bf16(uint32_t v) { return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u)); }
 
 KB_DEVI uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

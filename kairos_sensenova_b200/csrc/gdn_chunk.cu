@@ -692,62 +692,87 @@ __global__ void __launch_bounds__(STATE_THREADS) gdn_state_kernel(Params p, cons
 }
 
 // ---------------------------------------------------------------------------
-// Kernel 2b: segment combine.  Grid (V / 32, N * H); 256 threads.  Start states
+// Kernel 2b: segment combine.  Grid (V / 8, N * H); 256 threads.  Start states
 // of the segments of one sequence, a short sequential scan in fp32:
 //   h_1 = B_0,  h_s = M_{s-1} h_{s-1} + B_{s-1}   (s = 2 .. nseg-1)
-// (B_0 already starts from the initial state).  Thread t owns rows
-// (t / 8) * RPT .. + RPT and columns 4 (t % 8) .. + 4 of the 32-column slice; the
-// transposed transition streams through shared memory 32 rows of k at a time.
+// (B_0 already starts from the initial state).  Thread t owns rows t/2 (+128 i)
+// and columns 4 (t % 2) .. + 4 of the CTA's 8-column slice.  The transposed
+// transitions stream through shared memory in 64-row chunks by bulk copies,
+// double-buffered: every chunk is issued two chunks ahead of its use, across
+// the step boundary.  Waits are bounded; on a timeout the scan stops and the
+// later start states are left unwritten.
 // ---------------------------------------------------------------------------
-constexpr int COMB_THREADS = 256, COMB_KB = 32;
+constexpr int COMB_THREADS = 256, COMB_COLS = 8, COMB_KCH = 64;
+
+template <int K>
+struct CombSmem {
+  float mt[2][COMB_KCH * K];     // rows k of M^T (k = the input index of the transition)
+  float hs[K * COMB_COLS];       // current start state slice
+  uint64_t full[2];
+};
 
 template <int K, int V>
 __global__ void __launch_bounds__(COMB_THREADS) gdn_seg_combine_kernel(Params p) {
-  constexpr int RPT = K / 32;
-  extern __shared__ __align__(16) float csm[];
-  float* hs = csm;                   // [K][32] current start state slice
-  float* mt = csm + K * 32;          // [COMB_KB][K] rows of M^T
-  const int nh = blockIdx.y, v0 = blockIdx.x * 32, tid = threadIdx.x;
-  const int nseg = p.nseg, r0 = (tid >> 3) * RPT, c0 = (tid & 7) * 4;
+  constexpr int RPT = K / 128, NKC = K / COMB_KCH;
+  constexpr uint32_t CH_BYTES = COMB_KCH * K * 4;
+  extern __shared__ __align__(16) unsigned char csm_raw[];
+  CombSmem<K>& sm = *reinterpret_cast<CombSmem<K>*>(csm_raw);
+  const int nh = blockIdx.y, v0 = blockIdx.x * COMB_COLS, tid = threadIdx.x;
+  const int nseg = p.nseg, rr = tid >> 1, c0 = (tid & 1) * 4;
   const size_t sKV = (size_t)K * V;
   const float* B = p.seg_b + (size_t)nh * nseg * sKV;
   const float* M = p.seg_m + (size_t)nh * nseg * K * K;
   float* Hs = p.seg_h + (size_t)nh * nseg * sKV;
-  float acc[RPT][4];
+  const int nch = (nseg - 2) * NKC;                 // chunks of M_1 .. M_{nseg-2}
+  auto issue = [&](int f) {                         // thread 0: chunk f into buffer f & 1
+    const int s = 1 + f / NKC, kc = f % NKC;
+    tc::mbar_expect_tx(&sm.full[f & 1], CH_BYTES);
+    tc::bulk_load(sm.mt[f & 1], M + (size_t)s * K * K + (size_t)kc * COMB_KCH * K, CH_BYTES, &sm.full[f & 1]);
+  };
+  if (tid == 0) {
+    tc::mbar_init(&sm.full[0], 1);
+    tc::mbar_init(&sm.full[1], 1);
+    tc::fence_barrier_init();
+    for (int f = 0; f < 2 && f < nch; ++f) issue(f);
+  }
+  __syncthreads();
+  int f = 0;
   for (int s = 1; s < nseg; ++s) {
+    float acc[RPT][4];
 #pragma unroll
     for (int i = 0; i < RPT; ++i) {
-      const float4 b = *reinterpret_cast<const float4*>(B + (size_t)(s - 1) * sKV + (size_t)(r0 + i) * V + v0 + c0);
+      const float4 b = *reinterpret_cast<const float4*>(B + (size_t)(s - 1) * sKV + (size_t)(rr + 128 * i) * V + v0 + c0);
       acc[i][0] = b.x; acc[i][1] = b.y; acc[i][2] = b.z; acc[i][3] = b.w;
     }
     if (s > 1) {
-      const float* Ms = M + (size_t)(s - 1) * K * K;
-      for (int kb = 0; kb < K; kb += COMB_KB) {
-        __syncthreads();
-        for (int i = tid * 4; i < COMB_KB * K; i += COMB_THREADS * 4)
-          *reinterpret_cast<float4*>(mt + i) = *reinterpret_cast<const float4*>(Ms + (size_t)kb * K + i);
-        __syncthreads();
-#pragma unroll 4
-        for (int k = 0; k < COMB_KB; ++k) {
-          const float4 hv = *reinterpret_cast<const float4*>(hs + (kb + k) * 32 + c0);
+      for (int kc = 0; kc < NKC; ++kc, ++f) {
+        if (!__syncthreads_and(tc::mbar_wait(&sm.full[f & 1], (f >> 1) & 1))) return;
+        const float* mt = sm.mt[f & 1];
+        const float* hk = sm.hs + kc * COMB_KCH * COMB_COLS + c0;
+#pragma unroll 8
+        for (int k = 0; k < COMB_KCH; ++k) {
+          const float4 hv = *reinterpret_cast<const float4*>(hk + k * COMB_COLS);
 #pragma unroll
           for (int i = 0; i < RPT; ++i) {
-            const float a = mt[k * K + r0 + i];
+            const float a = mt[k * K + rr + 128 * i];
             acc[i][0] = fmaf(a, hv.x, acc[i][0]);
             acc[i][1] = fmaf(a, hv.y, acc[i][1]);
             acc[i][2] = fmaf(a, hv.z, acc[i][2]);
             acc[i][3] = fmaf(a, hv.w, acc[i][3]);
           }
         }
+        __syncthreads();                            // buffer f & 1 fully read
+        if (tid == 0 && f + 2 < nch) issue(f + 2);
       }
     }
-    __syncthreads();   // every read of hs of the previous step is done
+    __syncthreads();                                // every read of hs of this step is done
 #pragma unroll
     for (int i = 0; i < RPT; ++i) {
       const float4 o = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
-      *reinterpret_cast<float4*>(hs + (r0 + i) * 32 + c0) = o;
-      *reinterpret_cast<float4*>(Hs + (size_t)s * sKV + (size_t)(r0 + i) * V + v0 + c0) = o;
+      *reinterpret_cast<float4*>(sm.hs + (rr + 128 * i) * COMB_COLS + c0) = o;
+      *reinterpret_cast<float4*>(Hs + (size_t)s * sKV + (size_t)(rr + 128 * i) * V + v0 + c0) = o;
     }
+    __syncthreads();
   }
 }
 
@@ -1015,9 +1040,9 @@ int launch_state(gdn::Params p, const gdn::StateMaps& maps, const StatePlan& sp,
   p.seg_mode = 1;
   gdn::gdn_state_kernel<K, V, BV><<<dim3((V + K) / BV, nh * sp.nseg), gdn::STATE_THREADS, s2, st>>>(p, maps);
   if (int e = check_launch("gdn_state_kernel (segment-local)")) return e;
-  const size_t sc = (size_t)(K * 32 + gdn::COMB_KB * K) * 4;
+  const size_t sc = sizeof(gdn::CombSmem<K>);
   cudaFuncSetAttribute(gdn::gdn_seg_combine_kernel<K, V>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sc);
-  gdn::gdn_seg_combine_kernel<K, V><<<dim3(V / 32, nh), gdn::COMB_THREADS, sc, st>>>(p);
+  gdn::gdn_seg_combine_kernel<K, V><<<dim3(V / gdn::COMB_COLS, nh), gdn::COMB_THREADS, sc, st>>>(p);
   if (int e = check_launch("gdn_seg_combine_kernel")) return e;
   p.seg_mode = 2;
   gdn::gdn_state_kernel<K, V, BV><<<dim3(V / BV, nh * sp.nseg), gdn::STATE_THREADS, s2, st>>>(p, maps);

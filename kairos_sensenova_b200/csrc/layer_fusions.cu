@@ -209,7 +209,10 @@ __global__ void __launch_bounds__(256) rmsnorm_gated_kernel(const __nv_bfloat16*
 // h = c / hd, so q/k can be read straight out of a destination-grouped projection.
 // One CTA per RR rows (all loads issued up front), one 8-channel vector per
 // thread and row (blockDim = dim / 8).
-constexpr int RR = 4;
+#ifndef KB_NORM_RR
+#define KB_NORM_RR 4
+#endif
+constexpr int RR = KB_NORM_RR;
 __global__ void rmsnorm_rope_kernel(const __nv_bfloat16* x, __nv_bfloat16* y, int rows, int dim, int hd, int64_t ld,
                                     int hpb, int64_t bstride, const float* __restrict__ w,
                                     const float* __restrict__ cs, float eps) {
@@ -271,29 +274,46 @@ __global__ void rmsnorm_rope_kernel(const __nv_bfloat16* x, __nv_bfloat16* y, in
 // kairos_dit.py:873-874, 929-933, 955-957 and Head.forward :1047-1052):
 //   x <- bf16(x + gate * r)                 (when r is given; gate NULL = 1)
 //   y  = bf16(LN(x) * m + a),  m = (mul_plus_one ? 1 + mul : mul)  (mul NULL: m = 1; add NULL: a = 0)
-// One CTA of dim/8 threads per RR rows; each thread holds 8 channels of a row in
+// One CTA of dim/8 threads per LR rows; each thread holds 8 channels of a row in
 // registers; mean and variance by two block reductions (two-pass, fp32).
 // ---------------------------------------------------------------------------
-__global__ void residual_ln_mod_kernel(__nv_bfloat16* x, const __nv_bfloat16* r, int rows, int dim, int64_t ldr,
-                                       const float* __restrict__ gate, const float* __restrict__ mul,
-                                       const float* __restrict__ add, int plus_one, float eps,
-                                       __nv_bfloat16* y) {
-  __shared__ float red[2][RR][32];
+// Rows per CTA of residual_ln_mod_kernel.  Each thread keeps its loads of all LR
+// rows in flight before the first store; with LR = 2 and at most 56 registers
+// three CTAs of 384 threads (3072 channels) fit on an SM.
+#ifndef KB_LN_ROWS
+#define KB_LN_ROWS 2
+#endif
+constexpr int LR = KB_LN_ROWS;
+#ifndef KB_LN_REGS
+#define KB_LN_REGS __maxnreg__(56)
+#endif
+__global__ void KB_LN_REGS residual_ln_mod_kernel(__nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ r, int rows,
+                                       int dim, int64_t ldr, const float* __restrict__ gate,
+                                       const float* __restrict__ mul, const float* __restrict__ add, int plus_one,
+                                       float eps, __nv_bfloat16* __restrict__ y) {
+  __shared__ float red[2][LR][32];
   const int c = threadIdx.x * 8, nw = (blockDim.x + 31) / 32, lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  float xv[RR][8];
+  // every load of the CTA's rows is issued before the first store (the residual
+  // is written back in place)
+  uint4 raw[LR], rr[LR];
+#pragma unroll
+  for (int q = 0; q < LR; ++q) {
+    const int t = blockIdx.x * LR + q;
+    raw[q] = rr[q] = make_uint4(0, 0, 0, 0);
+    if (t < rows) {
+      raw[q] = *reinterpret_cast<const uint4*>(x + (int64_t)t * dim + c);
+      if (r) rr[q] = *reinterpret_cast<const uint4*>(r + (int64_t)t * ldr + c);
+    }
+  }
   float gv[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) gv[j] = gate ? gate[c + j] : 1.f;
+  float xv[LR][8];
 #pragma unroll
-  for (int q = 0; q < RR; ++q) {
-    const int t = blockIdx.x * RR + q;
-    uint4 raw = make_uint4(0, 0, 0, 0), rr = raw;
-    if (t < rows) {
-      raw = *reinterpret_cast<const uint4*>(x + (int64_t)t * dim + c);
-      if (r) rr = *reinterpret_cast<const uint4*>(r + (int64_t)t * ldr + c);
-    }
-    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
-    const __nv_bfloat16* er = reinterpret_cast<const __nv_bfloat16*>(&rr);
+  for (int q = 0; q < LR; ++q) {
+    const int t = blockIdx.x * LR + q;
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw[q]);
+    const __nv_bfloat16* er = reinterpret_cast<const __nv_bfloat16*>(&rr[q]);
     float s = 0.f;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
@@ -313,9 +333,9 @@ __global__ void residual_ln_mod_kernel(__nv_bfloat16* x, const __nv_bfloat16* r,
     if (lane == 0) red[0][q][wid] = s;
   }
   __syncthreads();
-  float mean[RR];
+  float mean[LR];
 #pragma unroll
-  for (int q = 0; q < RR; ++q) {
+  for (int q = 0; q < LR; ++q) {
     float tot = 0.f;
     for (int i = 0; i < nw; ++i) tot += red[0][q][i];
     mean[q] = tot / dim;
@@ -333,8 +353,8 @@ __global__ void residual_ln_mod_kernel(__nv_bfloat16* x, const __nv_bfloat16* r,
     av[j] = add ? add[c + j] : 0.f;
   }
 #pragma unroll
-  for (int q = 0; q < RR; ++q) {
-    const int t = blockIdx.x * RR + q;
+  for (int q = 0; q < LR; ++q) {
+    const int t = blockIdx.x * LR + q;
     if (t >= rows) continue;
     float tot = 0.f;
     for (int i = 0; i < nw; ++i) tot += red[1][q][i];
@@ -346,6 +366,165 @@ __global__ void residual_ln_mod_kernel(__nv_bfloat16* x, const __nv_bfloat16* r,
       ov[j / 2] = pack_bf16(fmaf((xv[q][j] - mean[q]) * rstd, mv[j], av[j]),
                             fmaf((xv[q][j + 1] - mean[q]) * rstd, mv[j + 1], av[j + 1]));
     *reinterpret_cast<uint4*>(y + (int64_t)t * dim + c) = o;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Warp-per-row forms of the two row norms for dim = 256 NV (NV vectors of 8
+// channels per lane; 3072 channels: NV = 12).  A warp owns a whole row, so no
+// block barrier separates a row's loads from its stores: every lane issues all
+// of its row's 16-byte loads up front and the warps of an SM stream
+// independently (the CTA-per-rows forms above stall all their warps at the
+// reduction barrier; they remain for other widths).
+// ---------------------------------------------------------------------------
+constexpr int WROWS = 8;   // rows (warps) per CTA
+
+template <int NV>
+__global__ void __launch_bounds__(WROWS * 32, 2) residual_ln_mod_warp_kernel(
+    __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ r, int rows, int64_t ldr,
+    const float* __restrict__ gate, const float* __restrict__ mul, const float* __restrict__ add, int plus_one,
+    float eps, __nv_bfloat16* __restrict__ y) {
+  constexpr int dim = 256 * NV;
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * WROWS + (threadIdx.x >> 5);
+  if (t >= rows) return;
+  __nv_bfloat16* xr = x + (int64_t)t * dim;
+  uint4 xv[NV], rv[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) xv[i] = *reinterpret_cast<const uint4*>(xr + (lane + 32 * i) * 8);
+  if (r) {
+#pragma unroll
+    for (int i = 0; i < NV; ++i) rv[i] = *reinterpret_cast<const uint4*>(r + (int64_t)t * ldr + (lane + 32 * i) * 8);
+  }
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = (lane + 32 * i) * 8;
+    uint32_t* xw = reinterpret_cast<uint32_t*>(&xv[i]);
+    if (r) {
+      const uint32_t* rw = reinterpret_cast<const uint32_t*>(&rv[i]);
+      float4 g0 = make_float4(1.f, 1.f, 1.f, 1.f), g1 = g0;
+      if (gate) {
+        g0 = *reinterpret_cast<const float4*>(gate + c);
+        g1 = *reinterpret_cast<const float4*>(gate + c + 4);
+      }
+      const float gg[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 a = unpack_bf16(xw[j]), b = unpack_bf16(rw[j]);
+        xw[j] = pack_bf16(fmaf(gg[2 * j], b.x, a.x), fmaf(gg[2 * j + 1], b.y, a.y));
+      }
+      *reinterpret_cast<uint4*>(xr + c) = xv[i];
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 a = unpack_bf16(xw[j]);
+      s += a.x + a.y;
+    }
+  }
+  const float mean = warp_sum(s) * (1.f / dim);
+  float s2 = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const uint32_t* xw = reinterpret_cast<const uint32_t*>(&xv[i]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 a = unpack_bf16(xw[j]);
+      s2 = fmaf(a.x - mean, a.x - mean, s2);
+      s2 = fmaf(a.y - mean, a.y - mean, s2);
+    }
+  }
+  const float rstd = rsqrtf(warp_sum(s2) * (1.f / dim) + eps);
+  __nv_bfloat16* yr = y + (int64_t)t * dim;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = (lane + 32 * i) * 8;
+    float mm[8], aa[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) { mm[j] = 1.f; aa[j] = 0.f; }
+    if (mul) {
+      const float4 m0 = *reinterpret_cast<const float4*>(mul + c), m1 = *reinterpret_cast<const float4*>(mul + c + 4);
+      mm[0] = m0.x; mm[1] = m0.y; mm[2] = m0.z; mm[3] = m0.w; mm[4] = m1.x; mm[5] = m1.y; mm[6] = m1.z; mm[7] = m1.w;
+      if (plus_one) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) mm[j] += 1.f;
+      }
+    }
+    if (add) {
+      const float4 a0 = *reinterpret_cast<const float4*>(add + c), a1 = *reinterpret_cast<const float4*>(add + c + 4);
+      aa[0] = a0.x; aa[1] = a0.y; aa[2] = a0.z; aa[3] = a0.w; aa[4] = a1.x; aa[5] = a1.y; aa[6] = a1.z; aa[7] = a1.w;
+    }
+    const uint32_t* xw = reinterpret_cast<const uint32_t*>(&xv[i]);
+    uint4 o;
+    uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 a = unpack_bf16(xw[j]);
+      ow[j] = pack_bf16(fmaf((a.x - mean) * rstd, mm[2 * j], aa[2 * j]),
+                        fmaf((a.y - mean) * rstd, mm[2 * j + 1], aa[2 * j + 1]));
+    }
+    *reinterpret_cast<uint4*>(yr + c) = o;
+    // keep the per-channel vector loads of the next vector below this store: hoisting
+    // all of them would not fit the register budget
+    asm volatile("" ::: "memory");
+  }
+}
+
+template <int NV>
+__global__ void __launch_bounds__(WROWS * 32, 2) rmsnorm_rope_warp_kernel(
+    const __nv_bfloat16* x, __nv_bfloat16* y, int rows, int hd, int64_t ld, int hpb, int64_t bstride,
+    const float* __restrict__ w, const float* __restrict__ cs, float eps) {
+  constexpr int dim = 256 * NV;
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * WROWS + (threadIdx.x >> 5);
+  if (t >= rows) return;
+  uint4 xv[NV];
+  auto offset = [&](int c) {
+    const int h = c / hd;
+    return (int64_t)(h / hpb) * bstride + (int64_t)(h % hpb) * hd + c % hd + (int64_t)t * ld;
+  };
+#pragma unroll
+  for (int i = 0; i < NV; ++i) xv[i] = *reinterpret_cast<const uint4*>(x + offset((lane + 32 * i) * 8));
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const uint32_t* xw = reinterpret_cast<const uint32_t*>(&xv[i]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 a = unpack_bf16(xw[j]);
+      ss = fmaf(a.x, a.x, fmaf(a.y, a.y, ss));
+    }
+  }
+  const float rstd = 1.f / sqrtf(warp_sum(ss) / dim + eps);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = (lane + 32 * i) * 8, cc = c % hd;
+    float wv[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) wv[j] = 1.f;
+    if (w) {
+      const float4 w0 = *reinterpret_cast<const float4*>(w + c), w1 = *reinterpret_cast<const float4*>(w + c + 4);
+      wv[0] = w0.x; wv[1] = w0.y; wv[2] = w0.z; wv[3] = w0.w; wv[4] = w1.x; wv[5] = w1.y; wv[6] = w1.z; wv[7] = w1.w;
+    }
+    float4 cs0 = make_float4(1.f, 0.f, 1.f, 0.f), cs1 = cs0;   // no table: identity rotation
+    if (cs) {
+      const float* csr = cs + ((int64_t)t * (hd / 2) + cc / 2) * 2;
+      cs0 = *reinterpret_cast<const float4*>(csr);
+      cs1 = *reinterpret_cast<const float4*>(csr + 4);
+    }
+    const float co[4] = {cs0.x, cs0.z, cs1.x, cs1.z}, si[4] = {cs0.y, cs0.w, cs1.y, cs1.w};
+    const uint32_t* xw = reinterpret_cast<const uint32_t*>(&xv[i]);
+    uint4 o;
+    uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 e = unpack_bf16(xw[j]);
+      const float a = bf16_round(e.x * rstd * wv[2 * j]);
+      const float b = bf16_round(e.y * rstd * wv[2 * j + 1]);
+      ow[j] = pack_bf16(a * co[j] - b * si[j], a * si[j] + b * co[j]);
+    }
+    *reinterpret_cast<uint4*>(y + offset(c)) = o;
+    asm volatile("" ::: "memory");   // as in residual_ln_mod_warp_kernel
   }
 }
 
@@ -431,6 +610,11 @@ extern "C" int kb200_rmsnorm_rope(const void* x, void* y, int64_t rows, int64_t 
   if (ld % 8 || block_stride % 8 || !aligned16(x) || !aligned16(y))
     return set_error(KB200_ERR_ALIGN, "rmsnorm_rope: rows must be 16-byte aligned");
   if (rows == 0) return KB200_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const unsigned wgrid = (unsigned)((rows + fuse::WROWS - 1) / fuse::WROWS);
+#define KB_RMS_WARP(NV)                                                                                       if (dim == 256 * NV) {                                                                                        fuse::rmsnorm_rope_warp_kernel<NV><<<wgrid, fuse::WROWS * 32, 0, st>>>(                                         (const __nv_bfloat16*)x, (__nv_bfloat16*)y, (int)rows, (int)head_dim, ld, (int)heads_per_block,             block_stride, weight, cos_sin, eps);                                                                    return check_launch("rmsnorm_rope_warp_kernel");                                                           }
+  KB_RMS_WARP(1) KB_RMS_WARP(2) KB_RMS_WARP(4) KB_RMS_WARP(8) KB_RMS_WARP(12)
+#undef KB_RMS_WARP
   fuse::rmsnorm_rope_kernel<<<(unsigned)((rows + fuse::RR - 1) / fuse::RR), (unsigned)(dim / 8), 0,
                                static_cast<cudaStream_t>(stream)>>>(
       (const __nv_bfloat16*)x, (__nv_bfloat16*)y, (int)rows, (int)dim, (int)head_dim, ld, (int)heads_per_block,
@@ -448,7 +632,12 @@ extern "C" int kb200_residual_ln_mod(void* x, const void* r, int64_t rows, int64
     return set_error(KB200_ERR_ALIGN, "residual_ln_mod: rows must be 16-byte aligned");
   if (x == y) return set_error(KB200_ERR_INVALID, "residual_ln_mod: y must not alias x");
   if (rows == 0) return KB200_OK;
-  fuse::residual_ln_mod_kernel<<<(unsigned)((rows + fuse::RR - 1) / fuse::RR), (unsigned)(dim / 8), 0,
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const unsigned wgrid = (unsigned)((rows + fuse::WROWS - 1) / fuse::WROWS);
+#define KB_LN_WARP(NV)                                                                                        if (dim == 256 * NV) {                                                                                        fuse::residual_ln_mod_warp_kernel<NV><<<wgrid, fuse::WROWS * 32, 0, st>>>(                                      (__nv_bfloat16*)x, (const __nv_bfloat16*)r, (int)rows, r ? ld_r : dim, gate, mul, add, mul_plus_one,         eps, (__nv_bfloat16*)y);                                                                                return check_launch("residual_ln_mod_warp_kernel");                                                        }
+  KB_LN_WARP(1) KB_LN_WARP(2) KB_LN_WARP(4) KB_LN_WARP(8) KB_LN_WARP(12)
+#undef KB_LN_WARP
+  fuse::residual_ln_mod_kernel<<<(unsigned)((rows + fuse::LR - 1) / fuse::LR), (unsigned)(dim / 8), 0,
                                  static_cast<cudaStream_t>(stream)>>>(
       (__nv_bfloat16*)x, (const __nv_bfloat16*)r, (int)rows, (int)dim, r ? ld_r : dim, gate, mul, add,
       mul_plus_one, eps, (__nv_bfloat16*)y);

@@ -131,10 +131,13 @@ class _Ulysses:
 
     def _project(self, x_local, W, b):
         """[Tl, hidden] -> [P, Tl, C] grouped by destination rank (+ bias)."""
-        x = x_local.unsqueeze(0)
         if b is None:
-            return torch.matmul(x, W)
-        return torch.baddbmm(b.unsqueeze(1), x.expand(self.P, -1, -1), W)
+            return torch.matmul(x_local.unsqueeze(0), W)
+        if self.P == 1:   # the bias in cuBLASLt's epilogue
+            return torch.addmm(b[0], x_local, W[0]).unsqueeze(0)
+        out = torch.matmul(x_local.unsqueeze(0), W)
+        out += b.unsqueeze(1)
+        return out
 
 
 class GdnMixer(_Ulysses):

@@ -3,6 +3,8 @@
     python -m kairos_sensenova_b200.profile_cases attn S H   # attention_fp8 on attn_inputs(1, S, H, 128, seed=1)
     python -m kairos_sensenova_b200.profile_cases gdn  T H   # chunk_gated_delta_rule on gdn_inputs(1, T, H, 128, 128, seed=0)
     python -m kairos_sensenova_b200.profile_cases prologue T H  # gdn_prologue on a fused [T, 3*H*128 + 2H (+pad)] projection
+    python -m kairos_sensenova_b200.profile_cases resln T C     # residual_ln_mod on [T, C] bf16 rows
+    python -m kairos_sensenova_b200.profile_cases dit L         # one eager DiT step (config 4 shapes, L blocks)
 
 Each runs the operator twice (warm) on synthetic seeded inputs and exits, so an
 ``ncu -k <kernel> -s <n> -c 1`` capture sees a handful of launches of a
@@ -44,8 +46,28 @@ def main(argv):
         for _ in range(2):
             gdn_prologue(s(0), s(1), s(2), proj[:, ab:ab + h], proj[:, ab + h:ab + 2 * h], w, w, w, A_log, dtb,
                          h, 1, n)
+    elif what == 'resln':
+        from .fused_ops import residual_ln_mod
+        gen = torch.Generator(device='cuda')
+        gen.manual_seed(0)
+        x = torch.randn(n, h, generator=gen, device='cuda').to(torch.bfloat16)
+        r = torch.randn(n, h, generator=gen, device='cuda').to(torch.bfloat16)
+        vec = [torch.randn(h, generator=gen, device='cuda') for _ in range(3)]
+        y = torch.empty_like(x)
+        for _ in range(2):
+            residual_ln_mod(x, r, vec[0], vec[1], vec[2], True, 1e-6, out=y)
+    elif what == 'dit':
+        from .dit import DiTConfig, KairosDiT
+        cfg = DiTConfig(layers=int(argv[2]) if len(argv) > 2 else 30)
+        model = KairosDiT(cfg)
+        gen = torch.Generator(device='cuda')
+        gen.manual_seed(2)
+        lat = torch.randn(cfg.in_dim, *cfg.latent, generator=gen, device='cuda')
+        ctx = torch.randn(cfg.text_len, cfg.text_dim, generator=gen, device='cuda')
+        with torch.no_grad():
+            model(lat, torch.tensor([500.0], device='cuda'), ctx)
     else:
-        raise SystemExit(f'unknown case {what!r} (attn | gdn | prologue)')
+        raise SystemExit(f'unknown case {what!r} (attn | gdn | prologue | resln | dit)')
     torch.cuda.synchronize()
     print('ok')
 

@@ -85,10 +85,11 @@ def test_gated_deltanet_layer_matches_oracle():
     assert max_rel(o, ref) < 2e-2
 
 
-def test_rmsnorm_rope_matches_reference_math():
+@pytest.mark.parametrize('H', [3, 4, 24])   # 384 channels: CTA-per-rows form; 512, 3072: warp-per-row form
+def test_rmsnorm_rope_matches_reference_math(H):
     from kairos_sensenova_b200.fused_ops import freqs_cis_3d, rmsnorm_rope, rope_table
     gen = torch.Generator().manual_seed(40)
-    H, D = 4, 128
+    D = 128
     fr = freqs_cis_3d(D, 3, 5, 7)                      # 105 tokens on a 3x5x7 grid
     S = fr.shape[0]
     x = (torch.randn(1, S, H * D, generator=gen) * 3).bfloat16()
@@ -98,11 +99,12 @@ def test_rmsnorm_rope_matches_reference_math():
     assert max_rel(y, ref) < 1e-2
 
 
-def test_rmsnorm_rope_in_place_on_grouped_projection():
+@pytest.mark.parametrize('P,Hl', [(2, 2), (8, 3)])
+def test_rmsnorm_rope_in_place_on_grouped_projection(P, Hl):
     """q as the first column block of a destination-grouped [P, T, 3*Hl*D] buffer."""
     from kairos_sensenova_b200.fused_ops import freqs_cis_3d, rmsnorm_rope, rope_table
     gen = torch.Generator().manual_seed(41)
-    P, Hl, D, T = 2, 2, 128, 60
+    D, T = 128, 60
     buf = torch.randn(P, T, 3 * Hl * D, generator=gen).bfloat16().cuda()
     fr = freqs_cis_3d(D, 3, 4, 5)
     cs = rope_table(fr, 'cuda')
