@@ -215,6 +215,8 @@ def main():
     ap.add_argument('--warmup', type=int, default=3)
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
     ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--eager', action='store_true',
+                    help='issue the hybrid step op by op instead of replaying it as one captured CUDA graph')
     ap.add_argument('--eager-dit', action='store_true',
                     help='time the DiT step issued op by op instead of as one captured CUDA graph')
     ap.add_argument('--dit-steps', type=int, default=3,
@@ -251,35 +253,55 @@ def main():
         for _ in range(args.warmup):
             blk.forward(x)
         sync_all()
+        # the attention kernel's own duration (roofline), CUDA events on its launch
+        # stream around the kernel, eager steps with the L2 flushed before each
+        aev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.steps)]
+        for a0, a1 in aev:
+            flush.zero_()
+            blk.forward(x, events=(a0, a1))
+        sync_all()
+        attn_ms = statistics.mean(a0.elapsed_time(a1) for a0, a1 in aev)
+        launches = blk.launches_per_step()
+        # the step: one CUDA graph per input buffer (two, ping-ponged by the e2e loop)
+        xd = [x.clone(), x.clone()]
+        if args.eager:
+            steps = [lambda b=b: blk.forward(xd[b]) for b in range(2)]
+        else:
+            from kairos_sensenova_b200.graphs import GraphedStep
+            steps = [GraphedStep(blk.forward, xd[b], static_inputs=True) for b in range(2)]
+        for _ in range(args.warmup):
+            steps[0]()
+        sync_all()
         sampler = ClockSampler(local) if rank == 0 else None
-        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
-               torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
               for _ in range(args.steps)]
         sync_all()
-        for s0, s1, a0, a1 in ev:
+        for s0, s1 in ev:
             flush.zero_()                       # L2 flush between timed steps (outside the events)
             s0.record()
-            blk.forward(x, events=(a0, a1))
+            steps[0]()
             s1.record()
         sync_all()
-        step_ms = statistics.mean(s0.elapsed_time(s1) for s0, s1, _, _ in ev)
-        launches = blk.launches_per_step()
-        attn_ms = statistics.mean(a0.elapsed_time(a1) for _, _, a0, a1 in ev)
+        step_ms = statistics.mean(s0.elapsed_time(s1) for s0, s1 in ev)
         # end to end through the public API with host buffers: every step copies its
-        # input from pinned host memory and its result back; copies run on a side
-        # stream, double-buffered, so step i's transfers overlap step i+-1's compute
+        # input from pinned host memory and its result back; the two directions run on
+        # their own streams (separate copy engines, full duplex), double-buffered, so
+        # step i's transfers overlap step i+-1's compute
         xh = [x.cpu().pin_memory() for _ in range(2)]
         yh = [torch.empty(Tl, HIDDEN, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
-        xd = [torch.empty_like(x) for _ in range(2)]
         comp = torch.cuda.current_stream()
-        copy = torch.cuda.Stream()
+        copy = torch.cuda.Stream()          # host -> device
+        back = torch.cuda.Stream()          # device -> host
         ev_in = [torch.cuda.Event() for _ in range(2)]
         ev_out = [torch.cuda.Event() for _ in range(2)]
         ev_free = [torch.cuda.Event() for _ in range(2)]
+        ev_read = [torch.cuda.Event() for _ in range(2)]
         sync_all()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(comp)
         copy.wait_event(e0)
+        back.wait_event(e0)
         with torch.cuda.stream(copy):
             xd[0].copy_(xh[0], non_blocking=True)
             ev_in[0].record(copy)
@@ -292,14 +314,19 @@ def main():
                     xd[(i + 1) % 2].copy_(xh[(i + 1) % 2], non_blocking=True)
                     ev_in[(i + 1) % 2].record(copy)
             comp.wait_event(ev_in[b_])
-            y = blk.forward(xd[b_])
+            if i >= 2:                      # step i-2's result has left this buffer's output
+                comp.wait_event(ev_read[b_])
+            y = steps[b_]()
             ev_free[b_].record(comp)
             ev_out[b_].record(comp)
-            with torch.cuda.stream(copy):
-                copy.wait_event(ev_out[b_])
+            with torch.cuda.stream(back):
+                back.wait_event(ev_out[b_])
                 yh[b_].copy_(y, non_blocking=True)
-                y.record_stream(copy)
+                ev_read[b_].record(back)
+            if args.eager:
+                y.record_stream(back)
         comp.wait_stream(copy)
+        comp.wait_stream(back)
         e1.record(comp)
         sync_all()
         e2e_ms = e0.elapsed_time(e1) / args.steps
@@ -329,6 +356,7 @@ def main():
                                    'hidden 3072, 24x128 heads, Ulysses over ranks',
                        'global_batch': 1, 'seq_len': T_FULL, 'parallelism': f'ulysses{world}',
                        'l2': 'flushed (256 MB write) between timed steps',
+                       'launch': 'eager' if args.eager else 'one CUDA graph per step',
                        'host_cpus_near_gpu': host_cpus},
             'e2e': {'value': T_FULL / (e2e_ms * 1e-3) / 1e6, 'unit': 'Mtokens/s',
                     'h2d_bytes_per_step': Tl * HIDDEN * 2, 'd2h_bytes_per_step': Tl * HIDDEN * 2},

@@ -19,11 +19,14 @@ import torch
 
 
 class GraphedStep:
-    def __init__(self, fn, *example_inputs, warmup: int = 2):
+    def __init__(self, fn, *example_inputs, warmup: int = 2, static_inputs: bool = False):
+        """``static_inputs=True`` makes the given tensors themselves the graph's
+        input buffers (the caller writes them, e.g. by its own copies) instead
+        of private clones."""
         if not all(isinstance(x, torch.Tensor) and x.is_cuda for x in example_inputs):
             raise ValueError('GraphedStep: inputs must be CUDA tensors')
         self.fn = fn
-        self.inputs = [x.clone() for x in example_inputs]
+        self.inputs = list(example_inputs) if static_inputs else [x.clone() for x in example_inputs]
         side = torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(side), torch.no_grad():
@@ -36,6 +39,7 @@ class GraphedStep:
             self.output = fn(*self.inputs)
 
     def __call__(self, *inputs):
+        """Copy ``inputs`` (if given) into the input buffers and replay."""
         for dst, src in zip(self.inputs, inputs):
             if src is not dst:
                 dst.copy_(src, non_blocking=True)
