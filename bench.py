@@ -216,7 +216,7 @@ def main():
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--eager', action='store_true',
-                    help='issue the hybrid step op by op instead of replaying it as one captured CUDA graph')
+                    help='issue the hybrid step op by op instead of replaying it as one captured CUDA graph (always so with more than one GPU)')
     ap.add_argument('--eager-dit', action='store_true',
                     help='time the DiT step issued op by op instead of as one captured CUDA graph')
     ap.add_argument('--dit-steps', type=int, default=3,
@@ -263,9 +263,15 @@ def main():
         sync_all()
         attn_ms = statistics.mean(a0.elapsed_time(a1) for a0, a1 in aev)
         launches = blk.launches_per_step()
-        # the step: one CUDA graph per input buffer (two, ping-ponged by the e2e loop)
+        # the step: one CUDA graph per input buffer (two, ping-ponged by the e2e loop).
+        # With more than one rank the step is issued op by op: in a 2-GPU run with the
+        # hybrid step's graphs (NCCL sends/receives captured inside) still alive at
+        # the end, a rank did not exit after its result was printed; the eager
+        # multi-rank path has always torn down cleanly, and at 2 GPUs both timed the
+        # same (10.2 vs 10.0 ms per step)
         xd = [x.clone(), x.clone()]
-        if args.eager:
+        eager = args.eager or world > 1
+        if eager:
             steps = [lambda b=b: blk.forward(xd[b]) for b in range(2)]
         else:
             from kairos_sensenova_b200.graphs import GraphedStep
@@ -323,7 +329,7 @@ def main():
                 back.wait_event(ev_out[b_])
                 yh[b_].copy_(y, non_blocking=True)
                 ev_read[b_].record(back)
-            if args.eager:
+            if eager:
                 y.record_stream(back)
         comp.wait_stream(copy)
         comp.wait_stream(back)
@@ -331,6 +337,8 @@ def main():
         sync_all()
         e2e_ms = e0.elapsed_time(e1) / args.steps
         clocks = sampler.stop() if sampler else None
+        del steps
+        torch.cuda.synchronize()
 
     del blk
     dit = time_dit(args, world, rank, sync_all, flush) if args.dit_steps > 0 else None
@@ -356,7 +364,7 @@ def main():
                                    'hidden 3072, 24x128 heads, Ulysses over ranks',
                        'global_batch': 1, 'seq_len': T_FULL, 'parallelism': f'ulysses{world}',
                        'l2': 'flushed (256 MB write) between timed steps',
-                       'launch': 'eager' if args.eager else 'one CUDA graph per step',
+                       'launch': 'eager' if eager else 'one CUDA graph per step',
                        'host_cpus_near_gpu': host_cpus},
             'e2e': {'value': T_FULL / (e2e_ms * 1e-3) / 1e6, 'unit': 'Mtokens/s',
                     'h2d_bytes_per_step': Tl * HIDDEN * 2, 'd2h_bytes_per_step': Tl * HIDDEN * 2},
