@@ -64,3 +64,26 @@ def test_python_op_rejects_cpu_and_grad():
     qg = q.clone().requires_grad_()
     with pytest.raises(NotImplementedError):
         chunk_gated_delta_rule(qg, q, q, q[..., 0], q[..., 0])
+
+
+def test_gdn_state_plan_launch_count(monkeypatch):
+    """The state-pass plan is host logic: 32-wide V slices and one segment for
+    many heads, 16-wide slices and concurrent segments (5 launches) for one
+    8-GPU rank's 3 heads, no segments for short or variable-length input.
+    (Without a GPU the plan assumes B200's 148 SMs.)"""
+    L = _lib.lib()
+    monkeypatch.delenv('KB200_GDN_SEGMENTS', raising=False)
+    monkeypatch.delenv('KB200_GDN_STATE_BV', raising=False)
+    cnt = lambda **kw: L.kb200_gdn_launch_count(ctypes.byref(_args(**kw)))  # noqa: E731
+    nt = lambda T: (T + 63) // 64  # noqa: E731
+    assert cnt(T=32760, H=24, num_chunks=nt(32760)) == 3
+    assert cnt(T=32760, H=3, num_chunks=nt(32760)) == 5
+    assert cnt(T=200, H=3, num_chunks=nt(200)) == 3
+    assert cnt(T=0, H=3, num_chunks=0) == 1           # no chunks: the state pass only (h0 -> ht)
+    assert cnt(K=96) == -1
+    seg = L.kb200_gdn_workspace_size(ctypes.byref(_args(T=32760, H=3, num_chunks=nt(32760))))
+    monkeypatch.setenv('KB200_GDN_SEGMENTS', '1')
+    assert cnt(T=32760, H=3, num_chunks=nt(32760)) == 3
+    one = L.kb200_gdn_workspace_size(ctypes.byref(_args(T=32760, H=3, num_chunks=nt(32760))))
+    # segments add the local end states, transitions and start states (fp32)
+    assert seg - one >= 3 * 6 * (128 * 128 * 4) * 3

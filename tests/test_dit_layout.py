@@ -1,0 +1,48 @@
+"""Host-side layout of the DiT step (no GPU): the patch embedding as a GEMM
+over flattened patches equals the reference's Conv3d, and unpatchify is the
+reference's rearrange (``kairos_dit.py:1167-1181``); the mixer patterns."""
+from types import SimpleNamespace
+
+import torch
+import torch.nn.functional as F
+from einops import rearrange
+
+from kairos_sensenova_b200.dit import DiTConfig, KairosDiT, sinusoidal_embedding_1d
+
+
+def _fake(cfg, world=1, rank=0):
+    return SimpleNamespace(cfg=cfg, P=world, rank=rank)
+
+
+def test_patchify_is_the_conv3d_patch_embedding():
+    cfg = DiTConfig(dim=32, heads=1, latent=(3, 8, 6))
+    gen = torch.Generator().manual_seed(0)
+    lat = torch.randn(cfg.in_dim, *cfg.latent, generator=gen)
+    W = torch.randn(cfg.dim, cfg.in_dim, *cfg.patch, generator=gen)
+    b = torch.randn(cfg.dim, generator=gen)
+    ref = F.conv3d(lat[None], W, b, stride=cfg.patch)[0].flatten(1).t()          # [T, dim]
+    p = KairosDiT._patchify(_fake(cfg), lat.bfloat16().float()).float()
+    got = p @ W.reshape(cfg.dim, -1).t() + b
+    ref2 = F.conv3d(lat.bfloat16().float()[None], W, b, stride=cfg.patch)[0].flatten(1).t()
+    assert got.shape == ref.shape == (cfg.tokens, cfg.dim)
+    assert torch.allclose(got, ref2, atol=1e-4, rtol=1e-4)
+    # each rank gets its contiguous token shard
+    shards = [KairosDiT._patchify(_fake(cfg, 2, r), lat) for r in range(2)]
+    assert torch.equal(torch.cat(shards), KairosDiT._patchify(_fake(cfg), lat))
+
+
+def test_unpatchify_is_the_reference_rearrange():
+    cfg = DiTConfig(dim=32, heads=1, latent=(3, 8, 6))
+    f, h, w = cfg.grid
+    y = torch.randn(f * h * w, cfg.out_dim * 4)
+    ref = rearrange(y[None], 'b (f h w) (x y z c) -> b c (f x) (h y) (w z)', f=f, h=h, w=w, x=1, y=2, z=2)[0]
+    assert torch.equal(KairosDiT._unpatchify(_fake(cfg), y), ref)
+
+
+def test_mixer_patterns_and_sinusoid():
+    base, ref = DiTConfig(layers=8), DiTConfig(layers=8, pattern='reference')
+    assert [base.is_gdn(i) for i in range(8)] == [True, True, True, False] * 2
+    assert [ref.is_gdn(i) for i in range(8)] == [False, False, False, True] * 2
+    e = sinusoidal_embedding_1d(256, torch.tensor([0.0, 500.0]))
+    assert e.shape == (2, 256) and torch.equal(e[0, :128], torch.ones(128, dtype=torch.float64))
+    assert abs(float(e[1, 0]) - float(torch.cos(torch.tensor(500.0, dtype=torch.float64)))) < 1e-12
