@@ -165,7 +165,12 @@ def residual_ln_mod(x: torch.Tensor, r, gate, mul, add, mul_plus_one: bool = Tru
     rows, dim = x.shape
     ldr = 0
     if r is not None:
+        if r.shape[-1] != dim or r.numel() != rows * dim:
+            raise ValueError(f'residual_ln_mod: r must hold [{rows}, {dim}], got {tuple(r.shape)}')
         r, ldr = _rows(r, dim)
+    for name, v in (('gate', gate), ('mul', mul), ('add', add)):
+        if v is not None and v.numel() != dim:
+            raise ValueError(f'residual_ln_mod: {name} must have {dim} elements, got {v.numel()}')
     if out is None:
         out = torch.empty_like(x)
     g, m, a = _vec(gate, dev), _vec(mul, dev), _vec(add, dev)

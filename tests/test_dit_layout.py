@@ -20,11 +20,10 @@ def test_patchify_is_the_conv3d_patch_embedding():
     lat = torch.randn(cfg.in_dim, *cfg.latent, generator=gen)
     W = torch.randn(cfg.dim, cfg.in_dim, *cfg.patch, generator=gen)
     b = torch.randn(cfg.dim, generator=gen)
-    ref = F.conv3d(lat[None], W, b, stride=cfg.patch)[0].flatten(1).t()          # [T, dim]
     p = KairosDiT._patchify(_fake(cfg), lat.bfloat16().float()).float()
     got = p @ W.reshape(cfg.dim, -1).t() + b
     ref2 = F.conv3d(lat.bfloat16().float()[None], W, b, stride=cfg.patch)[0].flatten(1).t()
-    assert got.shape == ref.shape == (cfg.tokens, cfg.dim)
+    assert got.shape == ref2.shape == (cfg.tokens, cfg.dim)
     assert torch.allclose(got, ref2, atol=1e-4, rtol=1e-4)
     # each rank gets its contiguous token shard
     shards = [KairosDiT._patchify(_fake(cfg, 2, r), lat) for r in range(2)]
