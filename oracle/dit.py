@@ -65,6 +65,45 @@ def cross_attention(b, y, ctx, H, eps):
     return _sdpa(q, k, v, H) @ b['Co'].t() + b['Cbo']
 
 
+def dit_block(b, x, ctx, t_mod, H, hd, eps, grid, gdn, ffn_act):
+    """``DiTBlock.forward`` (``kairos_dit.py:823-972``) for one sequence, fp32:
+    x [T, D], ctx [L, D] (already text-embedded), t_mod [6, D]; ``b`` holds the
+    block's weights in the layout of ``kairos_sensenova_b200.dit.make_weights``."""
+    m = b['mod'] + t_mod                                           # :864-882
+    y = _ln(x, eps) * (1 + m[0]) + m[1]                            # scale_msa, shift_msa: :873-874
+    if gdn:
+        mix = gdn_chain(b, y, H, hd, eps)
+    else:
+        mix = self_attention(b, y, H, hd, grid, eps)
+    x = x + m[2] * mix                                             # gate_msa: :929
+    x = x + cross_attention(b, _ln(x, eps) * b['ca_w'] + b['ca_b'], ctx, H, eps)   # :931-933
+    y = _ln(x, eps) * (1 + m[3]) + m[4]                            # scale, shift: :950-957
+    h = y @ b['W1'].t() + b['b1']
+    h = F.gelu(h, approximate='tanh') if ffn_act == 'gelu_tanh' else F.silu(h)
+    return x + m[5] * (h @ b['W2'].t() + b['b2'])                 # gate: :958-968
+
+
+REFERENCE_BLOCK_KEYS = {
+    'modulation': 'mod',
+    'self_attn.q.weight': 'Aq', 'self_attn.q.bias': 'Abq', 'self_attn.k.weight': 'Ak', 'self_attn.k.bias': 'Abk',
+    'self_attn.v.weight': 'Av', 'self_attn.v.bias': 'Abv', 'self_attn.o.weight': 'Ao', 'self_attn.o.bias': 'Abo',
+    'self_attn.norm_q.weight': 'nq', 'self_attn.norm_k.weight': 'nk',
+    'cross_attn.q.weight': 'Cq', 'cross_attn.q.bias': 'Cbq', 'cross_attn.k.weight': 'Ck', 'cross_attn.k.bias': 'Cbk',
+    'cross_attn.v.weight': 'Cv', 'cross_attn.v.bias': 'Cbv', 'cross_attn.o.weight': 'Co', 'cross_attn.o.bias': 'Cbo',
+    'cross_attn.norm_q.weight': 'Cnq', 'cross_attn.norm_k.weight': 'Cnk',
+    'cross_attn_norm.weight': 'ca_w', 'cross_attn_norm.bias': 'ca_b',
+    'ffn.0.weight': 'W1', 'ffn.0.bias': 'b1', 'ffn.2.weight': 'W2', 'ffn.2.bias': 'b2',
+}
+
+
+def block_weights_from_reference(state_dict):
+    """A reference ``DiTBlock`` state dict (softmax-attention block) in the
+    layout of ``make_weights``'s per-block dicts."""
+    b = {REFERENCE_BLOCK_KEYS[k]: v for k, v in state_dict.items() if k in REFERENCE_BLOCK_KEYS}
+    b['mod'] = b['mod'].reshape(6, -1)
+    return b
+
+
 def dit_forward(weights, cfg, latent, timestep, context):
     """latent [in_dim, F, H, W], timestep [1], context [text_len, text_dim] -> [out_dim, F, H, W] fp32."""
     w = {k: _f(v) for k, v in weights.items() if k != 'blocks'}
@@ -84,18 +123,7 @@ def dit_forward(weights, cfg, latent, timestep, context):
     x = x.flatten(1).t()                                                             # [T, D]
     for i, braw in enumerate(weights['blocks']):
         b = {k: _f(v) for k, v in braw.items()}
-        m = b['mod'] + t_mod
-        y = _ln(x, eps) * (1 + m[0]) + m[1]
-        if cfg.is_gdn(i):
-            mix = gdn_chain(b, y, H, hd, eps)
-        else:
-            mix = self_attention(b, y, H, hd, tuple(grid), eps)
-        x = x + m[2] * mix
-        x = x + cross_attention(b, _ln(x, eps) * b['ca_w'] + b['ca_b'], ctx, H, eps)
-        y = _ln(x, eps) * (1 + m[3]) + m[4]
-        h = y @ b['W1'].t() + b['b1']
-        h = F.gelu(h, approximate='tanh') if cfg.ffn_act == 'gelu_tanh' else F.silu(h)
-        x = x + m[5] * (h @ b['W2'].t() + b['b2'])
+        x = dit_block(b, x, ctx, t_mod, H, hd, eps, tuple(grid), cfg.is_gdn(i), cfg.ffn_act)
     shift, scale = w['head_mod'] + t
     out = (_ln(x, eps) * (1 + scale) + shift) @ w['head_w'].t() + w['head_b']        # [T, pf ph pw c]
     f_, h_, w_ = grid

@@ -45,3 +45,21 @@ def test_mixer_patterns_and_sinusoid():
     e = sinusoidal_embedding_1d(256, torch.tensor([0.0, 500.0]))
     assert e.shape == (2, 256) and torch.equal(e[0, :128], torch.ones(128, dtype=torch.float64))
     assert abs(float(e[1, 0]) - float(torch.cos(torch.tensor(500.0, dtype=torch.float64)))) < 1e-12
+
+
+def test_oracle_block_matches_reference_dit_block():
+    """The DiT oracle's block against the reference's own ``DiTBlock`` run on
+    CPU (fixture from ``tests/golden/make_dit_golden.py``): modulation order,
+    gated residuals, cross-attention norms and FFN are the reference's.  The
+    oracle rounds the normalised, rotated q/k to bf16 as the GPU path does
+    (the reference's fp32 run does not); agreement is ~3e-5, while swapping
+    scale and shift or the FFN activation moves the output by 2e-3 - 3e-3."""
+    from conftest import GOLDEN
+    from oracle.dit import block_weights_from_reference, dit_block
+    d = torch.load(GOLDEN / 'dit_block_attn.pt')
+    b = block_weights_from_reference(d['state_dict'])
+    H, D = d['heads'], d['dim']
+    y = dit_block(b, d['x'][0], d['context'][0], d['t_mod'][0], H, D // H, d['eps'], d['grid'], False, 'silu')
+    ref = d['out'][0]
+    err = float((y - ref).abs().max() / ref.abs().max())
+    assert err < 5e-4, err
