@@ -76,3 +76,17 @@ def test_oracle_varlen_equals_batched():
     o, s = og.gdn_chunk_varlen(q, k, v, g, beta, cu, None, None, True, True)
     oa, sa = og.gdn_chunk(q[:, :T1], k[:, :T1], v[:, :T1], g[:, :T1], beta[:, :T1], None, None, True, True)
     assert torch.allclose(o[:, :T1], oa, atol=1e-6) and torch.allclose(s[:1], sa, atol=1e-6)
+
+
+def test_layer_oracle_matches_reference_gated_deltanet_layer():
+    """The GatedDeltaNet layer oracle (short convolutions + SiLU, gates, chunk
+    op, gated RMSNorm, projections) against the reference's own vendored layer
+    run on CPU (fixture from ``tests/golden/make_layer_golden.py``)."""
+    import torch
+    from oracle import layers as ol
+    d = torch.load(__import__('conftest').GOLDEN / 'layer_gdn.pt')
+    y = ol.gated_deltanet_forward(d['state_dict'], d['x'], d['heads'], d['head_dim'], d['head_dim'],
+                                  d['norm_eps'], emulate_bf16=False)
+    ref = d['out']
+    err = float((y - ref).abs().max() / ref.abs().max())
+    assert err < 1e-4, err
