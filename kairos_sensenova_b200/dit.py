@@ -34,7 +34,7 @@ dilated variants are not implemented.
 from __future__ import annotations
 
 import math
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 
 import torch
 import torch.distributed as dist
@@ -61,7 +61,6 @@ class DiTConfig:
     pattern: str = 'baseline'          # 'baseline' | 'reference'
     ffn_act: str = 'gelu_tanh'         # 'gelu_tanh' | 'silu'
     conv_size: int = 4
-    extra: dict = field(default_factory=dict)
 
     @property
     def head_dim(self):
