@@ -20,6 +20,7 @@ port of the reference's torch code) on this host's cores, rank 0 only.
 from __future__ import annotations
 
 import argparse
+import datetime
 import json
 import os
 import statistics
@@ -46,14 +47,38 @@ def _peaks():
     return 1590.0, 6650.0, 'fallback'
 
 
-def _cpu_sample_seconds(reps=1):
-    """Time one bounded CPU sample: the hybrid chain for 1 of the 24 heads over
-    the full sequence (the per-head share of every projection included), with
-    the oracle restatement of the reference's torch code.  Returns seconds."""
-    from oracle.hybrid import attn_chain, gdn_chain
+def _cpu_model():
+    try:
+        for line in subprocess.run(['lscpu'], capture_output=True, text=True, timeout=10).stdout.splitlines():
+            if line.startswith('Model name:'):
+                return line.split(':', 1)[1].strip()
+    except (OSError, subprocess.SubprocessError):
+        pass
+    return None
+
+
+def _cpu_step_seconds(runs, warmup=1):
+    """Time the FULL config-3 hybrid step (both chains, all 24 heads, T = 32760,
+    every projection) on the host cores with the oracle restatement of the
+    reference's torch path (fp32, all threads): ``warmup`` untimed runs, then
+    ``runs`` timed ones.  Returns the list of seconds per run."""
+    from oracle.hybrid import attn_chain, freqs_cis_3d, gdn_chain
     torch.set_num_threads(os.cpu_count())
+    w, x = _cpu_inputs()
+    fr = freqs_cis_3d(HEAD_DIM, 21, 30, 52)
+    times = []
+    with torch.no_grad():
+        for i in range(warmup + runs):
+            t0 = time.perf_counter()
+            y = gdn_chain(w, x, HEADS, HEAD_DIM)
+            attn_chain(w, y, HEADS, HEAD_DIM, freqs=fr)
+            if i >= warmup:
+                times.append(time.perf_counter() - t0)
+    return times
+
+
+def _cpu_inputs():
     g = torch.Generator().manual_seed(0)
-    H, D = HEADS, HEAD_DIM
     w = {n: torch.randn(HEADS * HEAD_DIM, HIDDEN, generator=g) * 0.02 for n in ('Wq', 'Wk', 'Wv', 'Wg', 'Aq', 'Ak', 'Av')}
     w['Wo'] = torch.randn(HIDDEN, HEADS * HEAD_DIM, generator=g) * 0.02
     w['Ao'] = torch.randn(HIDDEN, HEADS * HEAD_DIM, generator=g) * 0.02
@@ -65,14 +90,7 @@ def _cpu_sample_seconds(reps=1):
     w['dt_bias'] = torch.randn(HEADS, generator=g) * 0.1 - 3
     w['o_norm_w'] = torch.ones(HEAD_DIM)
     x = torch.randn(T_FULL, HIDDEN, generator=g).bfloat16().float()
-    times = []
-    for _ in range(reps):
-        t0 = time.perf_counter()
-        with torch.no_grad():
-            y = gdn_chain(w, x, H, D, heads=[0])
-            attn_chain(w, y, H, D, heads=[0], work_share=True)
-        times.append(time.perf_counter() - t0)
-    return times
+    return w, x
 
 
 class ClockSampler:
@@ -116,24 +134,34 @@ class ClockSampler:
                 'reasons': sorted(reasons), 'samples': len(sm)}
 
 
+def _config(world):
+    return {'workload': 'config3 hybrid block: GDN chain + FP8-attention chain, T=32760, '
+                        'hidden 3072, 24x128 heads, Ulysses over ranks',
+            'global_batch': 1, 'seq_len': T_FULL, 'parallelism': f'ulysses{world}'}
+
+
 def run_reference(args, rank):
+    """The reference arm: the reference's CPU torch path for the whole config-3
+    step (the oracle port: the reference's path is Python/Triton and cannot run
+    on the GPU box), rank 0 only.  Each timed run is one FULL step -- nothing is
+    sampled or extrapolated; one untimed warm-up, then min(steps, 3) timed runs
+    (a full step takes tens of seconds on the host), reported as their median."""
     if rank != 0:
         return
-    times = _cpu_sample_seconds(args.warmup + args.steps)[args.warmup:]
-    step_s = statistics.mean(times) * HEADS        # the sample is 1/24 of a step's work
+    runs = max(1, min(args.steps, 3))
+    times = _cpu_step_seconds(runs, warmup=1)
+    step_s = statistics.median(times)
     v = T_FULL / step_s / 1e6
-    cores = os.cpu_count()
+    cores = torch.get_num_threads()
+    cpu = {'value': v, 'unit': 'Mtokens/s', 'cores': cores, 'kind': 'port', 'cpu_model': _cpu_model(),
+           'sample': f'the full config-3 step (all 24 heads, T=32760), fp32 oracle port of the reference torch '
+                     f'path; 1 warm-up + median of {runs} timed full steps; not extrapolated'}
     line = {
         'impl': 'reference', 'metric': METRIC, 'value': v, 'unit': 'Mtokens/s',
-        'n_gpus': args.gpus, 'steps': args.steps, 'warmup': args.warmup,
-        'ms_per_step': step_s * 1e3, 'higher_is_better': True, 'scaling': 'strong',
-        'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
-        'config': {'workload': 'config3 hybrid block (GDN chain + attention chain), T=32760, '
-                               'hidden 3072, 24x128 heads', 'global_batch': 1, 'seq_len': T_FULL,
-                   'parallelism': 'cpu'},
-        'cpu_baseline': {'value': v, 'unit': 'Mtokens/s', 'cores': cores, 'kind': 'port',
-                         'sample': 'hybrid chain for 1 of 24 heads over the full T=32760 '
-                                   '(per-head share of all projections), x24'},
+        'n_gpus': args.gpus, 'steps': runs, 'steps_requested': args.steps, 'warmup': 1,
+        'warmup_requested': args.warmup, 'ms_per_step': step_s * 1e3, 'run_ms': [t * 1e3 for t in times],
+        'higher_is_better': True, 'scaling': 'strong', 'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
+        'extrapolated': False, 'config': _config(args.gpus), 'cpu_baseline': cpu,
         'e2e': {'value': v, 'unit': 'Mtokens/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
     }
     print(json.dumps(line), flush=True)
@@ -158,6 +186,58 @@ def _bind_host_cpus(local_rank):
     except Exception:
         return None
     return None
+
+
+GDN_BYTES = 811.0e6          # config 1 compulsory HBM bytes: q,k,v,o bf16, g fp32, beta bf16, final state fp32
+GDN_FLOPS = 1.438e11         # config 1 algorithmic flops (182,955 per token-head x 786,240 token-heads)
+
+
+def time_gdn_op(flush, steps):
+    """the GDN chunk forward alone, B1 T32760 H24 d128, bf16
+    q/k/v/beta, fp32 g, fp32 final state, inputs resident in HBM (q, k already
+    L2-normalised as the config says).  CUDA events on the launch stream per
+    call, L2 flushed before each; returns the mean ms."""
+    from kairos_sensenova_b200 import chunk_gated_delta_rule
+    gen = torch.Generator(device='cuda')
+    gen.manual_seed(0)
+    B, T, H, K = 1, T_FULL, HEADS, HEAD_DIM
+    nrm = torch.nn.functional.normalize
+    q = nrm(torch.randn(B, T, H, K, generator=gen, device='cuda'), dim=-1).bfloat16()
+    k = nrm(torch.randn(B, T, H, K, generator=gen, device='cuda'), dim=-1).bfloat16()
+    v = torch.randn(B, T, H, K, generator=gen, device='cuda').bfloat16()
+    beta = torch.randn(B, T, H, generator=gen, device='cuda').sigmoid().bfloat16()
+    g = -torch.nn.functional.softplus(torch.randn(B, T, H, generator=gen, device='cuda'))
+    run = lambda: chunk_gated_delta_rule(q, k, v, g, beta, output_final_state=True)  # noqa: E731
+    for _ in range(3):
+        run()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for e0, e1 in ev:
+        flush.zero_()
+        e0.record()
+        run()
+        e1.record()
+    torch.cuda.synchronize()
+    return statistics.mean(e0.elapsed_time(e1) for e0, e1 in ev), chunk_gated_delta_rule.launches
+
+
+def time_sdpa_bf16(flush, steps):
+    """torch's bf16 SDPA (the library flash kernel) on config 2's shape
+    (B1 H24 S32760 d128, non-causal): the attention kernel's library baseline,
+    timed like it (CUDA events, L2 flushed)."""
+    gen = torch.Generator(device='cuda')
+    gen.manual_seed(1)
+    q, k, v = (torch.randn(1, HEADS, T_FULL, HEAD_DIM, generator=gen, device='cuda').bfloat16() for _ in range(3))
+    F = torch.nn.functional
+    for _ in range(2):
+        F.scaled_dot_product_attention(q, k, v)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for e0, e1 in ev:
+        flush.zero_()
+        e0.record()
+        F.scaled_dot_product_attention(q, k, v)
+        e1.record()
+    torch.cuda.synchronize()
+    return statistics.mean(e0.elapsed_time(e1) for e0, e1 in ev)
 
 
 def time_dit(args, world, rank, sync_all, flush):
@@ -219,6 +299,8 @@ def main():
                     help='issue the hybrid step op by op instead of replaying it as one captured CUDA graph (always so with more than one GPU)')
     ap.add_argument('--eager-dit', action='store_true',
                     help='time the DiT step issued op by op instead of as one captured CUDA graph')
+    ap.add_argument('--nccl-timeout', type=int, default=300,
+                    help='seconds before a collective that a peer never joins fails (NCCL process group timeout)')
     ap.add_argument('--dit-steps', type=int, default=3,
                     help='timed DiT denoise steps (BASELINE config 4) after the hybrid block; 0 skips')
     args = ap.parse_args()
@@ -231,7 +313,10 @@ def main():
     torch.cuda.set_device(local)
     host_cpus = _bind_host_cpus(local)
     if world > 1:
-        dist.init_process_group('nccl', device_id=torch.device('cuda', local))
+        # a bounded communicator timeout: a rank that never joins a collective ends the
+        # others' wait with an error instead of a hang
+        dist.init_process_group('nccl', device_id=torch.device('cuda', local),
+                                timeout=datetime.timedelta(seconds=args.nccl_timeout))
     from kairos_sensenova_b200.hybrid import HybridBlock
     assert T_FULL % world == 0 and HEADS % world == 0
     Tl = T_FULL // world
@@ -341,6 +426,13 @@ def main():
         torch.cuda.synchronize()
 
     del blk
+    gdn_ms = sdpa_ms = gdn_launches = None
+    if rank == 0:
+        torch.cuda.empty_cache()
+        gdn_ms, gdn_launches = time_gdn_op(flush, args.steps)
+        sdpa_ms = time_sdpa_bf16(flush, args.steps)
+        torch.cuda.empty_cache()
+    sync_all()
     dit = time_dit(args, world, rank, sync_all, flush) if args.dit_steps > 0 else None
     t = torch.tensor([step_ms, attn_ms, e2e_ms, dit['ms_per_step'] if dit else 0.0], device='cuda')
     if world > 1:
@@ -355,14 +447,14 @@ def main():
         units = T_FULL * (HEADS // world)
         traffic = 33.86e6 * units / (8192 * 8) + 2.0 * units * HEAD_DIM
         achieved = flops / (attn_ms * 1e-3) / 1e12
+        gdn_gbs = GDN_BYTES / (gdn_ms * 1e-3) / 1e9
+        gdn_tf = GDN_FLOPS / (gdn_ms * 1e-3) / 1e12
         line = {
             'metric': METRIC, 'value': T_FULL / (step_ms * 1e-3) / 1e6, 'unit': 'Mtokens/s',
             'n_gpus': world, 'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': step_ms,
             'higher_is_better': True, 'scaling': 'strong', 'vs_baseline': None, 'dtype': 'bf16/e4m3',
             'data': 'synthetic',
-            'config': {'workload': 'config3 hybrid block: GDN chain + FP8-attention chain, T=32760, '
-                                   'hidden 3072, 24x128 heads, Ulysses over ranks',
-                       'global_batch': 1, 'seq_len': T_FULL, 'parallelism': f'ulysses{world}',
+            'config': {**_config(world),
                        'l2': 'flushed (256 MB write) between timed steps',
                        'launch': 'eager' if eager else 'one CUDA graph per step',
                        'host_cpus_near_gpu': host_cpus},
@@ -372,22 +464,29 @@ def main():
             'roofline': {'kernel': 'attention (e4m3 QK, bf16 PV)',
                          'bound': 'tensor', 'achieved': achieved,
                          'peak': fp8_peak, 'unit': 'TFLOP/s', 'frac': achieved / fp8_peak,
-                         'traffic': traffic, 'attn_ms': attn_ms,
-                         'traffic_source': 'ncu dram read bytes of a B1 S8192 H8 capture (33.86 MB) scaled by '
-                                           'tokens x heads, plus the bf16 output bytes',
+                         'traffic': traffic, 'attn_ms': attn_ms, 'sdpa_bf16_ms': sdpa_ms,
+                         'traffic_source': 'ESTIMATE: ncu dram read bytes of a B1 S8192 H8 capture (33.86 MB) '
+                                           'scaled linearly by tokens x heads, plus the bf16 output bytes',
+                         'sdpa_source': 'torch bf16 scaled_dot_product_attention, config-2 shape, same run',
                          'peak_source': f'{kind} bf16 dense ({bf16_tf} TFLOP/s) x 4/3: QK at 2x (e4m3), PV at 1x (bf16)'},
+            'roofline_gdn': {'kernel': 'GDN chunk forward (config 1: B1 T32760 H24 d128)', 'bound': 'hbm',
+                             'gdn_ms': gdn_ms, 'launches': gdn_launches,
+                             'achieved': gdn_gbs, 'peak': hbm, 'unit': 'GB/s', 'frac': gdn_gbs / hbm,
+                             'algorithmic_bytes': GDN_BYTES, 'tflops': gdn_tf,
+                             'tensor_frac': gdn_tf / bf16_tf,
+                             'peak_source': f'{kind} HBM copy bandwidth; tensor_frac against {kind} bf16 dense'},
             'clocks': clocks,
         }
         if dit:
             dit['ms_per_step'] = dit_ms
             line['dit_step'] = dit
         if world == 1 and not args.no_cpu_baseline:
-            ts = _cpu_sample_seconds(2)
-            s = min(ts) * HEADS
-            line['cpu_baseline'] = {'value': T_FULL / s / 1e6, 'unit': 'Mtokens/s', 'cores': os.cpu_count(),
-                                    'kind': 'port',
-                                    'sample': 'oracle hybrid chain, 1 of 24 heads over the full T=32760 '
-                                              '(per-head share of all projections), scaled x24'}
+            ts = _cpu_step_seconds(1, warmup=0)
+            line['cpu_baseline'] = {'value': T_FULL / ts[0] / 1e6, 'unit': 'Mtokens/s',
+                                    'cores': torch.get_num_threads(), 'kind': 'port', 'cpu_model': _cpu_model(),
+                                    'ms_per_step': ts[0] * 1e3,
+                                    'sample': 'one full config-3 step (all 24 heads, T=32760), fp32 oracle port '
+                                              'of the reference torch path, no warm-up; not extrapolated'}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

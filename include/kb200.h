@@ -75,6 +75,11 @@ int kb200_gdn_launch_count(const KB200GdnArgs* a);
 /* Launch the forward.  `workspace` must be 256-byte aligned. */
 int kb200_gdn_chunk_fwd(const KB200GdnArgs* a, void* workspace, size_t workspace_bytes,
                         void* stream);
+/* Synchronises `stream` and reports KB200_ERR_TIMEOUT if a bounded device-side
+ * wait of the last kb200_gdn_chunk_fwd on `workspace` gave up (the kernels then
+ * record the site, let their copies in flight land and stop instead of hanging;
+ * later chunks' outputs are left unwritten).  No counterpart in the reference. */
+int kb200_gdn_status(const void* workspace, void* stream);
 
 /* Allocation-free variant of kb200_gdn_chunk_fwd (no counterpart in the
  * reference).  For callers that cannot allocate device memory when they run
@@ -82,11 +87,13 @@ int kb200_gdn_chunk_fwd(const KB200GdnArgs* a, void* workspace, size_t workspace
  * callback): the scratch comes from a 64 MiB array compiled into this
  * library, which every GPU that loads the library keeps until process exit.
  * Problems needing more scratch than kb200_gdn_noalloc_scratch_bytes()
- * are rejected with KB200_ERR_WORKSPACE.  The first call on a device looks up
- * the array's device address (cudaGetSymbolAddress) with that device
- * current; make that first call before any stream capture.  All calls share
+ * are rejected with KB200_ERR_WORKSPACE.  Every call looks up the array's
+ * device address (cudaGetSymbolAddress) on the current device; make the first
+ * call on a device before any stream capture (it may initialise the module).  All calls share
  * the one array: calls that overlap on the GPU (different streams, or
  * different threads on one device) race and must be serialised by the caller.
+ * The array's device address is looked up on every call, so the entry point
+ * stays valid after cudaDeviceReset (the array's contents do not survive it).
  * Nothing in the array needs to start at zero, so stale contents from an
  * earlier call do not matter.  Makes no cudaMalloc/cudaFree call. */
 size_t kb200_gdn_noalloc_scratch_bytes(void);
@@ -166,6 +173,11 @@ typedef struct KB200GdnPrologueArgs {
   int64_t B, T, H, Cqk, Cv;
   int W;                                             /* conv width, 1..4                     */
   int allow_neg_eigval;
+  /* Conv states carried from the previous piece of the sequence (ShortConvolution's
+   * `cache`, fla/modules/convolution.py:801-853): bf16 [B, C, W], column W-1 the
+   * input just before token 0, column W-1-j the one j tokens earlier; NULL = zeros
+   * (sequence start).  The new state (the last W inputs) is the caller's to form. */
+  const void* cache_q; const void* cache_k; const void* cache_v;
 } KB200GdnPrologueArgs;
 int kb200_gdn_prologue(const KB200GdnPrologueArgs* a, void* stream);
 
@@ -195,6 +207,18 @@ int kb200_rmsnorm_gated(const void* x, const void* gate, const float* weight, vo
 int kb200_residual_ln_mod(void* x, const void* r, int64_t rows, int64_t dim, int64_t ld_r,
                           const float* gate, const float* mul, const float* add, int mul_plus_one,
                           float eps, void* y, void* stream);
+
+/* ---------------------------------------------------------------------
+ * Failure-path test hooks (no counterpart in the reference).
+ * kb200_wait_probe: one CTA waits on an mbarrier nothing arrives on, with the
+ * bounded wait every kernel here uses and a budget of `budget_cycles` SM
+ * clocks (<= 4e9), then records site 99 in the device int `err_word` (zeroed
+ * first) -- the error path of a wait that runs out, with nothing in flight.
+ * kb200_read_error_word: synchronises `stream`, returns KB200_ERR_TIMEOUT if
+ * `err_word` holds a site code, KB200_OK if it is 0.
+ * --------------------------------------------------------------------- */
+int kb200_wait_probe(void* err_word, int64_t budget_cycles, void* stream);
+int kb200_read_error_word(const void* err_word, void* stream);
 
 #ifdef __cplusplus
 }

@@ -16,6 +16,7 @@ _lib = None
 KB200_OK = 0
 ERRORS = {1: 'invalid argument', 2: 'misaligned pointer', 3: 'workspace', 4: 'launch failure',
           5: 'device wait timed out'}
+ERRORS_BY_NAME = {'invalid': 1, 'align': 2, 'workspace': 3, 'launch': 4, 'timeout': 5}
 
 
 class GdnArgs(ctypes.Structure):
@@ -47,6 +48,7 @@ class GdnPrologueArgs(ctypes.Structure):
         ('B', ctypes.c_int64), ('T', ctypes.c_int64), ('H', ctypes.c_int64),
         ('Cqk', ctypes.c_int64), ('Cv', ctypes.c_int64),
         ('W', ctypes.c_int), ('allow_neg_eigval', ctypes.c_int),
+        ('cache_q', ctypes.c_void_p), ('cache_k', ctypes.c_void_p), ('cache_v', ctypes.c_void_p),
     ]
 
 
@@ -63,6 +65,9 @@ SIGNATURES = {
                                            ctypes.c_size_t, ctypes.c_void_p]),
     'kb200_rmsnorm_rope': (ctypes.c_int, [ctypes.c_void_p] * 2 + [ctypes.c_int64] * 6 +
                            [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_float, ctypes.c_void_p]),
+    'kb200_gdn_status': (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
+    'kb200_wait_probe': (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p]),
+    'kb200_read_error_word': (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
     'kb200_gdn_noalloc_scratch_bytes': (ctypes.c_size_t, []),
     'kb200_gdn_chunk_fwd_noalloc': (ctypes.c_int, [ctypes.POINTER(GdnArgs), ctypes.c_void_p]),
     'kb200_attn_fp8_workspace_size': (ctypes.c_size_t, [ctypes.c_int64] * 4),

@@ -22,7 +22,11 @@
 // operand reads already need.
 //
 // Every mbarrier wait is bounded; a wait that gives up records an error code in
-// the workspace and the CTA skips the rest of its work, frees TMEM and exits.
+// the workspace and the CTA skips the rest of its work.  Before it exits, the
+// producers wait (bounded) for the last TMA load of every ring slot and each MMA
+// issuer for all of its MMAs (one final commit); only then is TMEM freed.  If
+// one of those drain waits gives up too, TMEM is left allocated rather than
+// freed under a running MMA.
 #include "attn_common.cuh"
 #include "kb200_internal.h"
 #include "tc_common.cuh"
@@ -65,8 +69,10 @@ struct TcSmem {
   uint64_t o_done[TC_QT];                       // one phase: every PV of the tile completed
   uint64_t xbar[TC_QT][4];                      // per (tile, lane quarter): the two key halves of a row exchange a value
   float xch[TC_QT][2][2][TC_BM];                // [tile][use parity][half][row]
+  uint64_t drain[TC_QT];                        // abort-safe exit: every MMA of issuer t completed
   uint32_t tmem_base;
   int abort_flag;
+  int keep_tmem;                                // a drain wait gave up: TMEM may still be written, do not free it
 };
 
 struct TcMaps {
@@ -151,8 +157,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_fp8_tc_kernel(const __grid
       tc::mbar_init(&sm.pv_done[i], 1);
       tc::mbar_init(&sm.o_done[i], 1);
       for (int w = 0; w < 4; ++w) tc::mbar_init(&sm.xbar[i][w], 64);
+      tc::mbar_init(&sm.drain[i], 1);
     }
     sm.abort_flag = 0;
+    sm.keep_tmem = 0;
     tc::fence_barrier_init();
   }
   if (warp == 17) {
@@ -172,25 +180,39 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_fp8_tc_kernel(const __grid
       tc::mbar_expect_tx(&sm.q_full, TC_QT * TC_BM * TC_D);
       for (int qt = 0; qt < TC_QT; ++qt)
         tc::tma_load_2d(sm.q[qt], &maps.q, &sm.q_full, 0, bh * p.S_pad + q0 + qt * TC_BM);
+      int issued = 0;
       for (int j = 0; j < ntiles; ++j) {
         const int st = j % KS, use = j / KS;
         if (j >= KS && !tc::mbar_wait(&sm.k_empty[st], (use - 1) & 1)) { fail(sm, err, 11); break; }
         if (sm.abort_flag) break;
         tc::mbar_expect_tx(&sm.k_full[st], TC_BN * TC_D);
         tc::tma_load_2d(sm.k[st], &maps.k, &sm.k_full[st], 0, bh * p.S_pad + j * TC_BN);
+        ++issued;
       }
+      // before the CTA may exit, every load it issued must have landed (on the normal
+      // path they all have; after an abort the last load of each slot may be in flight)
+      bool drained = tc::mbar_wait(&sm.q_full, 0);
+      for (int j = issued > KS ? issued - KS : 0; j < issued; ++j)
+        drained &= tc::mbar_wait(&sm.k_full[j % KS], (j / KS) & 1);
+      if (!drained) { fail(sm, err, 18); sm.keep_tmem = 1; }
     }
   } else if (warp == 18) {
     // ------------------------------------------------------------ TMA producer of V^T
     if (lane == 0) {
       tc::prefetch_tmap(&maps.vt);
+      int issued = 0;
       for (int j = 0; j < ntiles; ++j) {
         const int st = j % VS, use = j / VS;
         if (j >= VS && !tc::mbar_wait(&sm.v_empty[st], (use - 1) & 1)) { fail(sm, err, 16); break; }
         if (sm.abort_flag) break;
         tc::mbar_expect_tx(&sm.v_full[st], 2 * TC_BN * TC_D);
         tc::tma_load_2d(sm.v[st], &maps.vt, &sm.v_full[st], j * TC_BN, bh * TC_D);
+        ++issued;
       }
+      bool drained = true;
+      for (int j = issued > VS ? issued - VS : 0; j < issued; ++j)
+        drained &= tc::mbar_wait(&sm.v_full[j % VS], (j / VS) & 1);
+      if (!drained) { fail(sm, err, 19); sm.keep_tmem = 1; }
     }
   } else if (warp == 17 || warp == 19) {
     // ------------------------------------------------------------ MMA issuers
@@ -238,6 +260,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_fp8_tc_kernel(const __grid
         }
       }
       if (ok) tc::tc_commit(&sm.o_done[qt]);
+      // every MMA this thread issued must complete before TMEM is freed (after an
+      // abort some may still be running)
+      tc::tc_commit(&sm.drain[qt]);
+      if (!tc::mbar_wait(&sm.drain[qt], 0)) { fail(sm, err, 20); sm.keep_tmem = 1; }
     }
   } else {
     // ------------------------------------------------------------ softmax (warps 0..15)
@@ -398,7 +424,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_fp8_tc_kernel(const __grid
   }
   tc::tc_fence_before();
   __syncthreads();
-  if (warp == 17) {
+  if (warp == 17 && !sm.keep_tmem) {
     tc::tc_fence_after();
     tc::tmem_dealloc(tmem, 512);
   }

@@ -22,5 +22,5 @@ int check_launch(const char* what) {
 }
 }  // namespace kb
 
-extern "C" int kb200_abi_version(void) { return 1; }
+extern "C" int kb200_abi_version(void) { return 2; }
 extern "C" const char* kb200_last_error(void) { return kb::g_err; }

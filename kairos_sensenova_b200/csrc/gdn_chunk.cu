@@ -59,6 +59,7 @@ struct Params {
   // transposed); seg_mode 2 runs every segment from its start state (seg_h, written
   // by the combine kernel) and writes the snapshots, v_new and the final state.
   int seg_mode, nseg, seg_chunks;
+  int* err;           // device error word: the site code of the first wait that gave up (0 = none)
   float* seg_b;       // [N*H, nseg, K, V]
   float* seg_m;       // [N*H, nseg, K(col), K(row)]
   float* seg_h;       // [N*H, nseg, K, V]
@@ -90,6 +91,10 @@ KB_DEVI ChunkLoc locate_chunk(const Params& p, int c) {
   if (p.cu_seqlens) {
     r.n = p.chunk_indices[2 * c];
     r.it = p.chunk_indices[2 * c + 1];
+    if (r.n < 0) {   // unused row of a table sized for the chunk-count upper bound
+      r.n = r.it = r.bos = r.len = 0;
+      return r;
+    }
     int s = p.cu_seqlens[r.n], e = p.cu_seqlens[r.n + 1];
     r.bos = s;
     r.len = min(BT, e - s - r.it * BT);
@@ -133,6 +138,7 @@ __global__ void __launch_bounds__(NTHREADS) gdn_prepare_kernel(Params p) {
   const int c = blockIdx.x, h = blockIdx.y, H = p.H;
   const ChunkLoc loc = locate_chunk(p, c);
   const int t0 = loc.bos + loc.it * BT, L = loc.len;
+  if (L <= 0) return;
 
   // ---- stage the chunk: every k, q, v row with cp.async at once (one memory round trip) ----
   {
@@ -574,9 +580,18 @@ __global__ void __launch_bounds__(STATE_THREADS) gdn_state_kernel(Params p, cons
       }
     STRACE(1, it);
     cp_async_wait<0>();
-    // bounded: on a timeout the pass stops here (outputs of later chunks are
-    // left unwritten) instead of hanging the GPU
-    if (!__syncthreads_and(tc::mbar_wait(&sm.full[buf], (li >> 1) & 1))) break;
+    // bounded: on a timeout the pass records the error and stops here (outputs of
+    // later chunks are left unwritten) instead of hanging the GPU.  The load it
+    // waited for is the only one in flight (the next is issued after this wait):
+    // wait for it once more, bounded, before the CTA may exit.
+    if (!__syncthreads_and(tc::mbar_wait(&sm.full[buf], (li >> 1) & 1))) {
+      if (tid == 0) {
+        atomicCAS(p.err, 0, 31);
+        tc::mbar_wait(&sm.full[buf], (li >> 1) & 1);
+      }
+      __syncthreads();
+      return;
+    }
     STRACE(2, it);
     STRACE(3, it);
     // snapshot -> global h[chunk] as coalesced 16-byte vectors
@@ -746,7 +761,15 @@ __global__ void __launch_bounds__(COMB_THREADS) gdn_seg_combine_kernel(Params p)
     }
     if (s > 1) {
       for (int kc = 0; kc < NKC; ++kc, ++f) {
-        if (!__syncthreads_and(tc::mbar_wait(&sm.full[f & 1], (f >> 1) & 1))) return;
+        if (!__syncthreads_and(tc::mbar_wait(&sm.full[f & 1], (f >> 1) & 1))) {
+          // record, then let the (at most two) bulk copies in flight land before exiting
+          if (tid == 0) {
+            atomicCAS(p.err, 0, 32);
+            for (int g = f; g < f + 2 && g < nch; ++g) tc::mbar_wait(&sm.full[g & 1], (g >> 1) & 1);
+          }
+          __syncthreads();
+          return;
+        }
         const float* mt = sm.mt[f & 1];
         const float* hk = sm.hs + kc * COMB_KCH * COMB_COLS + c0;
 #pragma unroll 8
@@ -799,6 +822,7 @@ __global__ void __launch_bounds__(NTHREADS) gdn_output_kernel(Params p) {
   const int v0 = blockIdx.x * BVO, c = blockIdx.y, h = blockIdx.z, H = p.H;
   const ChunkLoc loc = locate_chunk(p, c);
   const int t0 = loc.bos + loc.it * BT, L = loc.len;
+  if (L <= 0) return;
   {
     constexpr int KV = K / 8, VV = BVO / 8;
     for (int idx = tid; idx < BT * KV; idx += NTHREADS) {
@@ -960,7 +984,7 @@ StatePlan state_plan(const KB200GdnArgs* a) {
   return s;
 }
 
-struct WsLayout { size_t qn, kn, gc, w, u, vnew, hs, seg_b, seg_m, seg_h, total; StatePlan sp; };
+struct WsLayout { size_t err, qn, kn, gc, w, u, vnew, hs, seg_b, seg_m, seg_h, total; StatePlan sp; };
 
 WsLayout ws_layout(const KB200GdnArgs* a) {
   const size_t TT = (size_t)a->B * a->T, H = a->H, K = a->K, V = a->V;
@@ -968,6 +992,7 @@ WsLayout ws_layout(const KB200GdnArgs* a) {
   size_t off = 0;
   auto take = [&](size_t bytes) { size_t o = off; off = align_up(off + bytes); return o; };
   const size_t nqk = a->use_qk_l2norm ? TT * H * K * 2 : 0;
+  L.err = take(16);
   L.qn = take(nqk);
   L.kn = take(nqk);
   L.gc = take(TT * H * 4);
@@ -1075,12 +1100,14 @@ int launch(const KB200GdnArgs* a, const WsLayout& L, char* ws, cudaStream_t st) 
   p.NT = (int)((a->T + 63) / 64);
   p.scale = a->scale;
   p.l2norm = a->use_qk_l2norm;
+  p.err = (int*)(ws + L.err);
   p.seg_b = (float*)(ws + L.seg_b);
   p.seg_m = (float*)(ws + L.seg_m);
   p.seg_h = (float*)(ws + L.seg_h);
   const int H = (int)a->H;
   const int nchunks = (int)a->num_chunks;
   constexpr int BV = 32, BVO = 64;
+  if (cudaMemsetAsync(p.err, 0, sizeof(int), st) != cudaSuccess) return check_launch("gdn error word reset");
   if (nchunks > 0) {
     const size_t s1 = sizeof(gdn::PrepSmem<K, V>);
     cudaFuncSetAttribute(gdn::gdn_prepare_kernel<K, V>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s1);
@@ -1108,6 +1135,17 @@ int launch(const KB200GdnArgs* a, const WsLayout& L, char* ws, cudaStream_t st) 
 extern "C" size_t kb200_gdn_workspace_size(const KB200GdnArgs* a) {
   if (validate(a) != KB200_OK) return 0;
   return ws_layout(a).total;
+}
+
+extern "C" int kb200_gdn_status(const void* workspace, void* stream) {
+  if (!workspace) return kb::set_error(KB200_ERR_INVALID, "gdn_status: null workspace");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int code = 0;
+  if (cudaMemcpyAsync(&code, workspace, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)
+    return check_launch("gdn_status");
+  if (code != 0) return kb::set_error(KB200_ERR_TIMEOUT, "gdn: a device-side wait gave up (site %d)", code);
+  return KB200_OK;
 }
 
 extern "C" int kb200_gdn_launch_count(const KB200GdnArgs* a) {
@@ -1149,31 +1187,20 @@ extern "C" int kb200_gdn_chunk_fwd(const KB200GdnArgs* a, void* workspace, size_
 // file-scope device array instead of a caller-provided workspace.  The array
 // lives in every GPU that loads this library until the process exits.
 // ===========================================================================
-#include <mutex>
 
 namespace {
 constexpr size_t kGdnNoAllocScratchBytes = size_t(64) << 20;   // 64 MiB per device
 static __device__ __align__(256) unsigned char g_gdn_noalloc_scratch[kGdnNoAllocScratchBytes];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_noalloc_mu;
-void* g_noalloc_ptr[kMaxDevices] = {};
-
-// Device address of the scratch array on the current device (looked up once per device).
+// Device address of the scratch array on the current device.  Looked up on every
+// call (cheap, allocates nothing), so it stays right after a device reset or a
+// re-created primary context.
 int noalloc_scratch(void** out) {
-  int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
-    return set_error(KB200_ERR_LAUNCH, "gdn_noalloc: no usable current CUDA device");
-  std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (!g_noalloc_ptr[dev]) {
-    void* p = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&p, g_gdn_noalloc_scratch);
-    if (e != cudaSuccess || !p)
-      return set_error(KB200_ERR_LAUNCH, "gdn_noalloc: cudaGetSymbolAddress failed: %s",
-                       cudaGetErrorString(e));
-    g_noalloc_ptr[dev] = p;
-  }
-  *out = g_noalloc_ptr[dev];
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_gdn_noalloc_scratch);
+  if (e != cudaSuccess || !p)
+    return set_error(KB200_ERR_LAUNCH, "gdn_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+  *out = p;
   return KB200_OK;
 }
 }  // namespace

@@ -23,6 +23,7 @@ struct ConvSet {
   __nv_bfloat16* y;
   int C;
   int64_t ldx, ldy;   // row strides in elements
+  const __nv_bfloat16* cache;  // [B, C, W] conv state (the last W inputs before token 0) or null
 };
 
 struct PrologueParams {
@@ -78,6 +79,18 @@ __global__ void __launch_bounds__(PTHREADS, 5) gdn_prologue_kernel(PrologueParam
     for (int idx = tid; idx < (PT + 3) * (PC / 8); idx += PTHREADS) {
       const int r = idx / (PC / 8), cv = (idx % (PC / 8)) * 8;
       const int t = tok0 - 3 + r;
+      if (t < 0 && cs.cache) {
+        // history rows from the conv state: input t (< 0) sits at state column W + t
+        alignas(16) __nv_bfloat16 hv[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int c = c0 + cv + j;
+          hv[j] = (c < cs.C && p.W + t >= 0) ? cs.cache[((size_t)bb * cs.C + c) * p.W + p.W + t]
+                                              : __float2bfloat16(0.f);
+        }
+        *reinterpret_cast<uint4*>(&tile[r][cv]) = *reinterpret_cast<const uint4*>(hv);
+        continue;
+      }
       const bool ok = t >= 0 && t < p.T && c0 + cv < cs.C;
       cp_async16(&tile[r][cv], xb + (size_t)(ok ? t : 0) * cs.ldx + (ok ? c0 + cv : 0), ok);
     }
@@ -547,13 +560,14 @@ extern "C" int kb200_gdn_prologue(const KB200GdnPrologueArgs* a, void* stream) {
   void* ys[3] = {a->q, a->k, a->v};
   const int64_t cs[3] = {a->Cqk, a->Cqk, a->Cv};
   const int64_t lx[3] = {a->ldq, a->ldk, a->ldv};
+  const void* cc[3] = {a->cache_q, a->cache_k, a->cache_v};
   int maxc = 0;
   for (int i = 0; i < 3; ++i) {
     if (!xs[i] || !ws[i] || !ys[i]) return set_error(KB200_ERR_INVALID, "gdn_prologue: null tensor");
     if (cs[i] <= 0 || cs[i] % 8 || lx[i] % 8 || !aligned16(xs[i]) || !aligned16(ys[i]))
       return set_error(KB200_ERR_ALIGN, "gdn_prologue: channels/strides must be multiples of 8, rows 16-byte aligned");
     p.set[i] = fuse::ConvSet{(const __nv_bfloat16*)xs[i], ws[i], bs[i], (__nv_bfloat16*)ys[i], (int)cs[i],
-                             lx[i], cs[i]};
+                             lx[i], cs[i], (const __nv_bfloat16*)cc[i]};
     maxc = maxc > (int)cs[i] ? maxc : (int)cs[i];
   }
   if (!a->a || !a->b || !a->A_log || !a->dt_bias || !a->g || !a->beta)

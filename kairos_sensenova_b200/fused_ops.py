@@ -33,9 +33,13 @@ def _rows(x, C):
 
 
 def gdn_prologue(xq, xk, xv, a, b, wq, wk, wv, A_log, dt_bias, num_heads, B, T,
-                 bq=None, bk=None, bv=None, allow_neg_eigval=False):
+                 bq=None, bk=None, bv=None, allow_neg_eigval=False, conv_cache=None):
     """xq/xk/xv: bf16 [B*T, C] row views (may be column slices of one fused
     projection), a/b: bf16 [B*T, H] row views, conv weights [C, W].
+    ``conv_cache``: optional ``(cq, ck, cv)`` conv states ``[B, C, W]`` of the
+    preceding piece of each sequence (ShortConvolution's ``cache``,
+    ``fla/modules/convolution.py:771-798``); their last W-1 columns are the
+    inputs just before token 0.  They are read, not updated.
     Returns q, k [B,T,H,Cqk/H], v [B,T,H,Cv/H] bf16, g fp32 [B,T,H], beta bf16 [B,T,H]."""
     dev = xq.device
     if dev.type != 'cuda':
@@ -59,11 +63,20 @@ def gdn_prologue(xq, xk, xv, a, b, wq, wk, wv, A_log, dt_bias, num_heads, B, T,
     g = torch.empty(B, T, H, device=dev, dtype=torch.float32)
     beta = torch.empty(B, T, H, device=dev, dtype=torch.bfloat16)
     p = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+    caches = [None, None, None]
+    if conv_cache is not None:
+        for i, (c, C) in enumerate(zip(conv_cache, (Cqk, Cqk, Cv))):
+            if c is None:
+                continue
+            if tuple(c.shape) != (B, C, W):
+                raise ValueError(f'gdn_prologue: conv state must be [{B},{C},{W}], got {tuple(c.shape)}')
+            caches[i] = c.to(device=dev, dtype=torch.bfloat16).contiguous()
     args = _lib.GdnPrologueArgs(
         xq=p(xq), xk=p(xk), xv=p(xv), ldq=ldq, ldk=ldk, ldv=ldv, wq=p(wq), wk=p(wk), wv=p(wv),
         bq=p(bq), bk=p(bk), bv=p(bv), q=p(q), k=p(k), v=p(v), a=p(a), b=p(b), lda=lda, ldb=ldb,
         A_log=p(A), dt_bias=p(dtb), g=p(g), beta=p(beta), B=B, T=T, H=H, Cqk=Cqk, Cv=Cv, W=W,
-        allow_neg_eigval=int(bool(allow_neg_eigval)))
+        allow_neg_eigval=int(bool(allow_neg_eigval)),
+        cache_q=p(caches[0]), cache_k=p(caches[1]), cache_v=p(caches[2]))
     with torch.cuda.device(dev):
         _lib.check(_lib.lib().kb200_gdn_prologue(ctypes.byref(args), _stream(dev)), 'gdn_prologue')
     return q, k, v, g, beta

@@ -14,9 +14,19 @@ Same signature, argument meaning, defaults and errors as the reference op
 
 Arithmetic: bf16 operands (q, k, v, beta, w, u, state snapshots) with fp32
 accumulation, fp32 gates and an fp32 running state -- the precision the
-reference's Triton kernels use for bf16 activations.  Inputs given in another
-float dtype are converted to bf16 first.  Only the forward exists: calling it
-with grad-requiring inputs under autograd raises ``NotImplementedError``.
+reference's Triton kernels use for bf16 activations.  q, k and v must be bf16:
+other dtypes raise ``ValueError`` (the reference would compute fp32 inputs in
+fp32; this op has no fp32 path, and silently rounding them would change the
+results).  g may be any float dtype (it is used in fp32, like the reference);
+beta is used in bf16 (fp32 beta is rounded, a 2^-9 relative change).  Only the
+forward exists: calling it with grad-requiring inputs under autograd raises
+``NotImplementedError``.  ``check=True`` (an extra keyword; the reference's
+``**kwargs`` ignores it) synchronises after the launch and raises
+``RuntimeError`` if a bounded device-side wait gave up.
+
+Variable-length input (``cu_seqlens``) needs no host synchronisation: the
+(sequence, chunk) table is built on the device for the upper bound
+``ceil(T/64) + N`` of the chunk count, with unused rows marked empty.
 """
 from __future__ import annotations
 
@@ -34,17 +44,27 @@ def _ptr(t):
     return None if t is None else t.data_ptr()
 
 
-def prepare_chunk_indices(cu_seqlens: torch.Tensor, chunk_size: int = BT):
-    """(seq, chunk) pairs and per-sequence chunk offsets for variable-length input
-    (the same tables as ``fla/ops/utils/index.py`` ``prepare_chunk_indices`` /
-    ``prepare_chunk_offsets``), built on the host."""
-    lens = (cu_seqlens[1:] - cu_seqlens[:-1]).tolist()
-    pairs, offs = [], [0]
-    for n, ln in enumerate(lens):
-        nt = (int(ln) + chunk_size - 1) // chunk_size
-        pairs.extend((n, i) for i in range(nt))
-        offs.append(offs[-1] + nt)
-    return pairs, offs
+def prepare_chunk_indices(cu_seqlens: torch.Tensor, total_tokens: int, chunk_size: int = BT):
+    """(sequence, chunk) rows and per-sequence chunk offsets for variable-length
+    input (the tables of ``fla/ops/utils/index.py`` ``prepare_chunk_indices`` /
+    ``prepare_chunk_offsets``), built with device ops only (no host sync).
+
+    Returns ``(indices [M, 2] int32, offsets [N+1] int32, M)`` with
+    ``M = ceil(total_tokens / chunk_size) + N`` -- an upper bound of the chunk
+    count known from shapes alone; rows past the real chunk count hold
+    sequence -1 and are skipped by the kernels."""
+    N = cu_seqlens.shape[0] - 1
+    M = (total_tokens + chunk_size - 1) // chunk_size + N
+    cu = cu_seqlens.to(torch.int64)
+    nt = (cu[1:] - cu[:-1] + chunk_size - 1) // chunk_size
+    offs = torch.cat([nt.new_zeros(1), torch.cumsum(nt, 0)])
+    c = torch.arange(M, device=cu.device, dtype=torch.int64)
+    n = torch.searchsorted(offs[1:].contiguous(), c, right=True)
+    valid = n < N
+    nc = n.clamp(max=max(N - 1, 0))
+    it = c - offs[nc]
+    idx = torch.stack([torch.where(valid, nc, torch.full_like(nc, -1)), torch.where(valid, it, 0)], 1)
+    return idx.to(torch.int32).contiguous(), offs.to(torch.int32).contiguous(), M
 
 
 @torch.compiler.disable
@@ -83,10 +103,10 @@ def chunk_gated_delta_rule(
             t is not None and t.requires_grad for t in (q, k, v, g, beta, initial_state)):
         raise NotImplementedError('kairos_sensenova_b200.chunk_gated_delta_rule is forward-only')
     return _forward(q, k, v, g, beta, float(scale), initial_state, output_final_state,
-                    cu_seqlens, use_qk_l2norm_in_kernel)
+                    cu_seqlens, use_qk_l2norm_in_kernel, bool(kwargs.get('check', False)))
 
 
-def _forward(q, k, v, g, beta, scale, initial_state, output_final_state, cu_seqlens, l2norm):
+def _forward(q, k, v, g, beta, scale, initial_state, output_final_state, cu_seqlens, l2norm, check=False):
     dev = q.device
     if dev.type != 'cuda':
         raise RuntimeError('chunk_gated_delta_rule: inputs must be CUDA tensors (no CPU path)')
@@ -96,19 +116,19 @@ def _forward(q, k, v, g, beta, scale, initial_state, output_final_state, cu_seql
     if k.shape != q.shape or v.shape[:3] != q.shape[:3] or g.shape != q.shape[:3] or beta.shape != q.shape[:3]:
         raise ValueError(f'chunk_gated_delta_rule: inconsistent shapes q{tuple(q.shape)} k{tuple(k.shape)} '
                          f'v{tuple(v.shape)} g{tuple(g.shape)} beta{tuple(beta.shape)}')
-    out_dtype = q.dtype
+    bf = torch.bfloat16
+    if q.dtype != bf or k.dtype != bf or v.dtype != bf:
+        raise ValueError(f'chunk_gated_delta_rule: q, k, v must be bfloat16 (this op computes in bf16 with fp32 '
+                         f'accumulation and has no fp32 path), got {q.dtype}, {k.dtype}, {v.dtype}')
     with torch.cuda.device(dev):
-        bf = torch.bfloat16
-        qc, kc, vc = (x.to(bf).contiguous() for x in (q, k, v))
+        qc, kc, vc = (x.contiguous() for x in (q, k, v))
         gc = g.to(torch.float32).contiguous()
         bc = beta.to(bf).contiguous()
         if cu_seqlens is not None:
-            pairs, offs = prepare_chunk_indices(cu_seqlens.cpu())
-            N = len(offs) - 1
-            nchunks = len(pairs)
-            cu32 = cu_seqlens.to(device=dev, dtype=torch.int32).contiguous()
-            ci = torch.tensor(pairs if pairs else [[0, 0]], dtype=torch.int32).reshape(-1, 2).to(dev)
-            co = torch.tensor(offs, dtype=torch.int32).to(dev)
+            cu_dev = cu_seqlens.to(device=dev)
+            ci, co, nchunks = prepare_chunk_indices(cu_dev, B * T)
+            N = cu_seqlens.shape[0] - 1
+            cu32 = cu_dev.to(torch.int32).contiguous()
         else:
             N = B
             nchunks = B * ((T + BT - 1) // BT)
@@ -133,6 +153,8 @@ def _forward(q, k, v, g, beta, scale, initial_state, output_final_state, cu_seql
         stream = torch.cuda.current_stream(dev).cuda_stream
         _lib.check(L.kb200_gdn_chunk_fwd(ctypes.byref(a), ws.data_ptr(), nbytes, stream),
                    'chunk_gated_delta_rule')
+        if check:   # synchronises; raises if a bounded device-side wait gave up
+            _lib.check(L.kb200_gdn_status(ws.data_ptr(), stream), 'chunk_gated_delta_rule')
         # kernel launches of the last call (launch accounting for benchmarks)
         chunk_gated_delta_rule.launches = L.kb200_gdn_launch_count(ctypes.byref(a))
-    return o.to(out_dtype), ht
+    return o, ht

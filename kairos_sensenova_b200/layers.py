@@ -9,8 +9,13 @@ use_cache=False, output_attentions=False, **kwargs) -> (o, None, past_key_values
 
 Projections are plain cuBLAS GEMMs (``nn.Linear``); the short convolutions,
 SiLU and gates run in one prologue kernel, the recurrence in the chunked GDN
-kernels and the gated RMSNorm in one epilogue kernel.  Padding masks and
-recurrent caches (``attention_mask``, ``past_key_values``/``use_cache``) are
+kernels and the gated RMSNorm in one epilogue kernel.  Recurrent caches work
+as in the reference (``gated_deltanet.py:225-253,273-305``): with
+``past_key_values`` the layer reads this layer's conv states (the last W raw
+q/k/v projection inputs) and recurrent state, continues the sequence from them,
+and with ``use_cache`` stores the new ones -- so a long sequence walked in
+pieces through one :class:`Cache` gives the one-shot result (the DiT block's
+GDN loop, ``kairos_dit.py:880-922``).  Padding masks (``attention_mask``) are
 not implemented and raise ``NotImplementedError``.  The reference routes
 ``q_len <= 64`` to its fused-recurrent kernel (``gated_deltanet.py:220``);
 the chunk kernels here are exact for every length, so they serve all lengths.
@@ -24,6 +29,75 @@ import torch.nn as nn
 
 from .fused_ops import gdn_prologue, rms_norm_gated
 from .gated_delta_rule import chunk_gated_delta_rule
+
+
+class Cache:
+    """Per-layer recurrent-state cache with the interface ``GatedDeltaNet`` uses
+    (``fla/models/utils.py:283-382``, ``FLACache``): ``len(cache)`` is the number of
+    layers that stored state, ``cache[i]`` that layer's dict (``recurrent_state``,
+    ``attn_state``, ``conv_state``, ``ffn_state``), ``update(..., layer_idx,
+    offset)`` stores new states (growing the layer list to ``layer_idx``) and counts
+    the tokens seen by layer 0."""
+
+    def __init__(self, seen_tokens: int = 0):
+        self.layers = []
+        self._seen_tokens = int(seen_tokens)
+
+    @classmethod
+    def from_legacy_cache(cls, past_key_values=None, seen_tokens: int = 0):
+        cache = cls(seen_tokens)
+        if isinstance(past_key_values, (list, tuple)):
+            cache.layers = [dict(st) for st in past_key_values]
+        return cache
+
+    def to_legacy_cache(self):
+        return tuple(self.layers)
+
+    def __len__(self):
+        return len(self.layers)
+
+    def __getitem__(self, layer_idx):
+        if layer_idx >= len(self.layers):
+            raise KeyError(f"Cache only have {len(self.layers)} layers, however accessed {layer_idx} out of bounds")
+        return self.layers[layer_idx]
+
+    def __iter__(self):
+        yield from self.layers
+
+    def update(self, recurrent_state=None, attn_state=None, conv_state=None, ffn_state=None, layer_idx=0,
+               offset=1, cache_kwargs=None):
+        while len(self.layers) <= layer_idx:
+            self.layers.append(dict(recurrent_state=None, attn_state=None, conv_state=None, ffn_state=None))
+        if layer_idx == 0:
+            self._seen_tokens += int(offset)
+        st = self.layers[layer_idx]
+        if recurrent_state is not None:
+            st['recurrent_state'] = recurrent_state
+        if attn_state is not None:
+            old = st['attn_state']
+            st['attn_state'] = tuple(attn_state) if old is None else tuple(
+                torch.cat([a, b], 1) for a, b in zip(old, attn_state))
+        if conv_state is not None:
+            st['conv_state'] = conv_state
+        if ffn_state is not None:
+            st['ffn_state'] = ffn_state
+        return st
+
+    def get_seq_length(self, layer_idx=0):
+        return self._seen_tokens if len(self.layers) > (layer_idx or 0) else 0
+
+
+def _next_conv_state(prev, x, W):
+    """The conv state after the piece ``x [B, T, C]``: the last W inputs of the
+    sequence so far, ``[B, C, W]`` (older ones from ``prev`` when T < W), as
+    ``causal_conv1d_states_fwd_kernel`` forms it (``fla/modules/convolution.py:534-577``)."""
+    B, T, C = x.shape
+    xt = x.transpose(1, 2)
+    if T >= W:
+        return xt[..., T - W:].contiguous()
+    if prev is None:
+        prev = x.new_zeros(B, C, W)
+    return torch.cat([prev.to(x.dtype), xt], -1)[..., -W:].contiguous()
 
 
 class ShortConvolution(nn.Conv1d):
@@ -103,19 +177,35 @@ class GatedDeltaNet(nn.Module):
                 output_attentions=False, **kwargs):
         if attention_mask is not None:
             raise NotImplementedError('padding masks are not implemented on this path')
-        if past_key_values is not None or use_cache:
-            raise NotImplementedError('recurrent caches are not implemented on this path')
         B, T, _ = hidden_states.shape
         H = self.num_heads
+        cu_seqlens = kwargs.get('cu_seqlens')
+        last_state = None
+        layer_idx = self.layer_idx or 0
+        if past_key_values is not None and len(past_key_values) > layer_idx:
+            last_state = past_key_values[layer_idx]
+        if last_state is not None and cu_seqlens is not None:
+            raise NotImplementedError('a conv cache together with cu_seqlens is not on this path')
+        conv_prev = last_state['conv_state'] if last_state is not None else None
         x2 = hidden_states.reshape(B * T, -1)
+        xq, xk, xv = self.q_proj(x2), self.k_proj(x2), self.v_proj(x2)
         cb = lambda c: None if c.bias is None else c.bias  # noqa: E731
         q, k, v, g, beta = gdn_prologue(
-            self.q_proj(x2), self.k_proj(x2), self.v_proj(x2), self.a_proj(x2), self.b_proj(x2),
+            xq, xk, xv, self.a_proj(x2), self.b_proj(x2),
             self.q_conv1d.weight[:, 0], self.k_conv1d.weight[:, 0], self.v_conv1d.weight[:, 0],
             self.A_log, self.dt_bias, H, B, T, cb(self.q_conv1d), cb(self.k_conv1d), cb(self.v_conv1d),
-            self.allow_neg_eigval)
-        o, _ = chunk_gated_delta_rule(q, k, v, g, beta, cu_seqlens=kwargs.get('cu_seqlens'),
-                                      use_qk_l2norm_in_kernel=True)
+            self.allow_neg_eigval, conv_cache=conv_prev)
+        recurrent_state = last_state['recurrent_state'] if last_state is not None else None
+        o, recurrent_state = chunk_gated_delta_rule(q, k, v, g, beta, initial_state=recurrent_state,
+                                                    output_final_state=use_cache, cu_seqlens=cu_seqlens,
+                                                    use_qk_l2norm_in_kernel=True)
+        if past_key_values is not None:
+            # as the reference: the conv states are only formed with use_cache
+            prev = conv_prev if conv_prev is not None else (None, None, None)
+            conv_state = tuple(_next_conv_state(p, x.reshape(B, T, -1), self.conv_size) if use_cache else None
+                               for p, x in zip(prev, (xq, xk, xv)))
+            past_key_values.update(recurrent_state=recurrent_state, conv_state=conv_state,
+                                   layer_idx=layer_idx, offset=T)
         gate = self.g_proj(x2).reshape(B, T, H, self.head_v_dim)
         o = self.o_norm(o, gate)
         o = self.o_proj(o.reshape(B, T, self.value_dim).to(hidden_states.dtype))

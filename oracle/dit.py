@@ -133,3 +133,59 @@ def dit_forward(weights, cfg, latent, timestep, context):
 
 def tokens_of(cfg):
     return math.prod(cfg.grid)
+
+
+def self_attention_rows(b, x, H, D, grid, eps, rows):
+    """``self_attention`` for the query rows ``[0, rows)`` only (keys and values
+    from every token): the exact values of those rows at a fraction of the cost."""
+    fr = freqs_cis_3d(D, *grid)
+    q = rmsnorm_rope((x[:rows] @ b['Aq'].t() + b['Abq'])[None], b['nq'], fr[:rows], H, eps)[0].float()
+    k = rmsnorm_rope((x @ b['Ak'].t() + b['Abk'])[None], b['nk'], fr, H, eps)[0].float()
+    v = x @ b['Av'].t() + b['Abv']
+    return _sdpa(q, k, v, H) @ b['Ao'].t() + b['Abo']
+
+
+def dit_forward_rows(weights, cfg, latent, timestep, context, rows):
+    """A ONE-block model (``cfg.layers == 1``) for the first ``rows`` tokens only:
+    returns the head output ``[rows, pf*ph*pw*out_dim]`` before unpatchify.
+    Exact for those rows -- everything but the mixer is per token, the
+    GatedDeltaNet mixer is causal (a prefix needs only the prefix) and the
+    attention mixer takes its keys and values from every token -- so a
+    full-size block can be checked without the full-sequence CPU cost."""
+    assert cfg.layers == 1
+    w = {k: _f(v) for k, v in weights.items() if k != 'blocks'}
+    D, H, hd, eps = cfg.dim, cfg.heads, cfg.head_dim, cfg.eps
+    half = cfg.freq_dim // 2
+    pos = timestep.double().cpu().reshape(-1)
+    s = torch.outer(pos, torch.pow(10000, -torch.arange(half, dtype=torch.float64).div(half)))
+    t_in = torch.cat([torch.cos(s), torch.sin(s)], 1).float()
+    t = F.silu(t_in @ w['time_w1'].t() + w['time_b1']) @ w['time_w2'].t() + w['time_b2']
+    t_mod = (F.silu(t) @ w['tproj_w'].t() + w['tproj_b']).reshape(6, D)
+    ctx = _f(context)
+    ctx = F.silu(ctx @ w['text_w1'].t() + w['text_b1']) @ w['text_w2'].t() + w['text_b2']
+    pf, ph, pw = cfg.patch
+    conv_w = w['patch_w'].reshape(D, cfg.in_dim, pf, ph, pw)
+    x = F.conv3d(_f(latent)[None], conv_w, w['patch_b'], stride=cfg.patch)[0]
+    grid = tuple(x.shape[1:])
+    x = x.flatten(1).t()                                                             # [T, D]
+    b = {k: _f(v) for k, v in weights['blocks'][0].items()}
+    m = b['mod'] + t_mod
+    gdn = cfg.is_gdn(0)
+    y = _ln(x if not gdn else x[:rows], eps) * (1 + m[0]) + m[1]
+    mix = gdn_chain(b, y, H, hd, eps) if gdn else self_attention_rows(b, y, H, hd, grid, eps, rows)
+    x = x[:rows] + m[2] * mix
+    x = x + cross_attention(b, _ln(x, eps) * b['ca_w'] + b['ca_b'], ctx, H, eps)
+    y = _ln(x, eps) * (1 + m[3]) + m[4]
+    h = y @ b['W1'].t() + b['b1']
+    h = F.gelu(h, approximate='tanh') if cfg.ffn_act == 'gelu_tanh' else F.silu(h)
+    x = x + m[5] * (h @ b['W2'].t() + b['b2'])
+    shift, scale = w['head_mod'] + t
+    return (_ln(x, eps) * (1 + scale) + shift) @ w['head_w'].t() + w['head_b']
+
+
+def patch_rows(velocity, cfg):
+    """Inverse of unpatchify: ``[c, F, H, W]`` -> ``[T, pf*ph*pw*c]`` token rows."""
+    f, h, w = cfg.grid
+    pf, ph, pw = cfg.patch
+    c = velocity.shape[0]
+    return velocity.reshape(c, f, pf, h, ph, w, pw).permute(1, 3, 5, 2, 4, 6, 0).reshape(f * h * w, -1)

@@ -25,7 +25,7 @@ def test_library_loads_and_exports_all_declared_symbols():
 
 
 def test_abi_version():
-    assert _lib.lib().kb200_abi_version() == 1
+    assert _lib.lib().kb200_abi_version() == 2
 
 
 def _args(**kw):

@@ -114,3 +114,40 @@ def test_rmsnorm_rope_in_place_on_grouped_projection(P, Hl):
                  block_stride=T * 3 * Hl * D)
     got = torch.cat([buf[r, :, :Hl * D] for r in range(P)], dim=1)
     assert torch.equal(got, ref)
+
+
+@pytest.mark.parametrize('pieces', [8, 'ragged'])
+def test_gated_deltanet_cache_walk_matches_one_shot(pieces):
+    """The DiT block's GDN loop (``kairos_dit.py:880-922``): the sequence walked in
+    pieces through one Cache with use_cache=True gives the one-shot output (conv
+    states carry the last W-1 projection inputs, the recurrent state carries
+    through ``initial_state``/``output_final_state``); the final recurrent state
+    equals the one-shot final state.  Tolerance 2e-2 max-relative."""
+    from kairos_sensenova_b200.layers import Cache, GatedDeltaNet
+    torch.manual_seed(1)
+    hidden, H, hd, T = 512, 4, 128, 640
+    layer = GatedDeltaNet(hidden_size=hidden, expand_v=1, head_dim=hd, num_heads=H, layer_idx=2)
+    with torch.no_grad():
+        for n, p_ in layer.named_parameters():
+            if n.endswith('proj.weight'):
+                p_.normal_(0, 0.02)
+    layer = layer.cuda().to(torch.bfloat16)
+    x = torch.randn(1, T, hidden, device='cuda').bfloat16()
+    with torch.no_grad():
+        full, _, c1 = layer(x, past_key_values=Cache(), use_cache=True)
+        bounds = list(range(0, T + 1, T // 8)) if pieces == 8 else [0, 1, 3, 67, 130, 131, 400, T]
+        cache = Cache.from_legacy_cache()
+        outs = []
+        for s, e in zip(bounds[:-1], bounds[1:]):
+            o, _, cache = layer(x[:, s:e].contiguous(), past_key_values=cache, use_cache=True)
+            outs.append(o)
+    walk = torch.cat(outs, 1)
+    assert max_rel(walk, full) < 2e-2
+    assert cache.get_seq_length(0) == 0 and len(cache) == 3          # layer 2's state only, as FLACache
+    assert max_rel(cache[2]['recurrent_state'], c1[2]['recurrent_state']) < 1e-2
+    for a, b in zip(cache[2]['conv_state'], c1[2]['conv_state']):
+        assert torch.equal(a, b)
+    # without a cache the layer is the one-shot call
+    with torch.no_grad():
+        o0, _, none = layer(x)
+    assert none is None and torch.equal(o0, full)

@@ -90,3 +90,22 @@ def test_layer_oracle_matches_reference_gated_deltanet_layer():
     ref = d['out']
     err = float((y - ref).abs().max() / ref.abs().max())
     assert err < 1e-4, err
+
+
+def test_dit_rows_oracle_equals_full_oracle_on_its_rows():
+    """oracle.dit.dit_forward_rows (used by the full-size config-4 block tests) is
+    exact for the rows it computes: checked against the full-sequence oracle on a
+    small one-block model of each mixer kind."""
+    from kairos_sensenova_b200.dit import DiTConfig, make_weights
+    from oracle.dit import dit_forward, dit_forward_rows, patch_rows
+    for pat in ('baseline', 'reference'):
+        cfg = DiTConfig(dim=256, heads=2, ffn_dim=512, layers=1, text_dim=64, text_len=16, latent=(4, 16, 16),
+                        pattern=pat)
+        w = make_weights(cfg, 'cpu', seed=2)
+        gen = torch.Generator().manual_seed(7)
+        lat = torch.randn(cfg.in_dim, *cfg.latent, generator=gen)
+        ctx = torch.randn(cfg.text_len, cfg.text_dim, generator=gen)
+        t = torch.tensor([500.0])
+        full = patch_rows(dit_forward(w, cfg, lat, t, ctx), cfg)
+        rows = dit_forward_rows(w, cfg, lat, t, ctx, 100)
+        assert (full[:100] - rows).abs().max() <= 1e-5 * full.abs().max()
