@@ -19,6 +19,7 @@
 #include "common.cuh"
 #include "kb200_internal.h"
 #include "tc_common.cuh"
+#include "gdn_tc.cuh"
 #include <type_traits>
 #include <cstring>
 #include <algorithm>
@@ -923,6 +924,26 @@ __global__ void __launch_bounds__(NTHREADS) gdn_output_kernel(Params p) {
 }
 
 }  // namespace gdn
+
+int gdn_seg_combine(float* seg_b, float* seg_m, float* seg_h, int nseg, int nh, int K, int V, int* err,
+                    cudaStream_t st) {
+  gdn::Params p{};
+  p.seg_b = seg_b;
+  p.seg_m = seg_m;
+  p.seg_h = seg_h;
+  p.nseg = nseg;
+  p.err = err;
+  auto go = [&](auto kern, int KK) {
+    const size_t sc = sizeof(gdn::CombSmem<128>) + (KK == 256 ? sizeof(gdn::CombSmem<256>) - sizeof(gdn::CombSmem<128>) : 0);
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sc);
+    kern<<<dim3(V / gdn::COMB_COLS, nh), gdn::COMB_THREADS, sc, st>>>(p);
+    return check_launch("gdn_seg_combine_kernel");
+  };
+  if (K == 128 && V == 128) return go(gdn::gdn_seg_combine_kernel<128, 128>, 128);
+  if (K == 128 && V == 256) return go(gdn::gdn_seg_combine_kernel<128, 256>, 128);
+  if (K == 128 && V == 512) return go(gdn::gdn_seg_combine_kernel<128, 512>, 128);
+  return set_error(KB200_ERR_INVALID, "gdn_seg_combine: unsupported dims");
+}
 }  // namespace kb
 
 // ===========================================================================
@@ -1130,11 +1151,29 @@ int launch(const KB200GdnArgs* a, const WsLayout& L, char* ws, cudaStream_t st) 
   }
   return KB200_OK;
 }
+
+// Head dim K = 128 (every configuration of the benchmarked path) runs the tcgen05
+// kernels of gdn_tc.cu; K = 256 runs the mma.sync kernels above.
+size_t gdn_ws_total(const KB200GdnArgs* a) {
+  return gdntc::supported(a) ? gdntc::layout(a).total : ws_layout(a).total;
+}
+
+int gdn_launch_any(const KB200GdnArgs* a, char* ws, cudaStream_t st) {
+  if (gdntc::supported(a)) return gdntc::launch(a, gdntc::layout(a), ws, st);
+  const WsLayout L = ws_layout(a);
+#define KB_GDN_CASE(KK, VV) \
+  if (a->K == KK && a->V == VV) return launch<KK, VV>(a, L, ws, st);
+  KB_GDN_CASE(256, 128)
+  KB_GDN_CASE(256, 256)
+  KB_GDN_CASE(256, 512)
+#undef KB_GDN_CASE
+  return kb::set_error(KB200_ERR_INVALID, "gdn: unsupported dims");
+}
 }  // namespace
 
 extern "C" size_t kb200_gdn_workspace_size(const KB200GdnArgs* a) {
   if (validate(a) != KB200_OK) return 0;
-  return ws_layout(a).total;
+  return gdn_ws_total(a);
 }
 
 extern "C" int kb200_gdn_status(const void* workspace, void* stream) {
@@ -1150,6 +1189,7 @@ extern "C" int kb200_gdn_status(const void* workspace, void* stream) {
 
 extern "C" int kb200_gdn_launch_count(const KB200GdnArgs* a) {
   if (validate(a) != KB200_OK) return -1;
+  if (gdntc::supported(a)) return gdntc::launch_count(a);
   const StatePlan sp = state_plan(a);
   return (a->num_chunks > 0 ? 2 : 0) + (sp.nseg > 1 ? 3 : 1);
 }
@@ -1157,24 +1197,12 @@ extern "C" int kb200_gdn_launch_count(const KB200GdnArgs* a) {
 extern "C" int kb200_gdn_chunk_fwd(const KB200GdnArgs* a, void* workspace, size_t workspace_bytes,
                                    void* stream) {
   if (int e = validate(a)) return e;
-  const WsLayout L = ws_layout(a);
-  if (!workspace || workspace_bytes < L.total)
-    return kb::set_error(KB200_ERR_WORKSPACE, "gdn: workspace needs %zu bytes, got %zu", L.total,
-                         workspace_bytes);
+  const size_t total = gdn_ws_total(a);
+  if (!workspace || workspace_bytes < total)
+    return kb::set_error(KB200_ERR_WORKSPACE, "gdn: workspace needs %zu bytes, got %zu", total, workspace_bytes);
   if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
     return kb::set_error(KB200_ERR_ALIGN, "gdn: workspace must be 256-byte aligned");
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  char* ws = static_cast<char*>(workspace);
-#define KB_GDN_CASE(KK, VV) \
-  if (a->K == KK && a->V == VV) return launch<KK, VV>(a, L, ws, st);
-  KB_GDN_CASE(128, 128)
-  KB_GDN_CASE(128, 256)
-  KB_GDN_CASE(128, 512)
-  KB_GDN_CASE(256, 128)
-  KB_GDN_CASE(256, 256)
-  KB_GDN_CASE(256, 512)
-#undef KB_GDN_CASE
-  return kb::set_error(KB200_ERR_INVALID, "gdn: unsupported dims");
+  return gdn_launch_any(a, static_cast<char*>(workspace), static_cast<cudaStream_t>(stream));
 }
 
 // ===========================================================================
@@ -1209,24 +1237,13 @@ extern "C" size_t kb200_gdn_noalloc_scratch_bytes(void) { return kGdnNoAllocScra
 
 extern "C" int kb200_gdn_chunk_fwd_noalloc(const KB200GdnArgs* a, void* stream) {
   if (int e = validate(a)) return e;
-  const WsLayout L = ws_layout(a);
-  if (L.total > kGdnNoAllocScratchBytes)
+  const size_t total = gdn_ws_total(a);
+  if (total > kGdnNoAllocScratchBytes)
     return kb::set_error(KB200_ERR_WORKSPACE,
                          "gdn_noalloc: problem needs %zu bytes of scratch, the built-in array "
                          "holds %zu; use kb200_gdn_chunk_fwd with a caller workspace",
-                         L.total, kGdnNoAllocScratchBytes);
+                         total, kGdnNoAllocScratchBytes);
   void* ws = nullptr;
   if (int e = noalloc_scratch(&ws)) return e;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  char* w = static_cast<char*>(ws);
-#define KB_GDN_CASE(KK, VV) \
-  if (a->K == KK && a->V == VV) return launch<KK, VV>(a, L, w, st);
-  KB_GDN_CASE(128, 128)
-  KB_GDN_CASE(128, 256)
-  KB_GDN_CASE(128, 512)
-  KB_GDN_CASE(256, 128)
-  KB_GDN_CASE(256, 256)
-  KB_GDN_CASE(256, 512)
-#undef KB_GDN_CASE
-  return kb::set_error(KB200_ERR_INVALID, "gdn_noalloc: unsupported dims");
+  return gdn_launch_any(a, static_cast<char*>(ws), static_cast<cudaStream_t>(stream));
 }

@@ -1,0 +1,1153 @@
+// gdn_tc.cu -- chunked gated delta rule forward on 5th-generation tensor cores
+// (tcgen05 + TMEM, TMA / bulk copies), sm_100a, head dim K = 128.
+//
+// Two kernels (plus the segment combine of gdn_chunk.cu when the state pass is
+// split into concurrent segments):
+//
+// 1. gdn_prep_tc_kernel -- one CTA per (64-token chunk, head), parallel:
+//      q, k, v tiles by TMA; optional L2 norm of q, k     (fla/modules/l2norm.py:98-130)
+//      in-chunk gate cumsum (warp scan)                    (fla/ops/utils/cumsum.py:27-65)
+//      S = K K^T and Q K^T on tcgen05 (M64 N64, bf16)      (fla/ops/common/chunk_scaled_dot_kkt.py:28-73)
+//      A = beta_i e^{g_i-g_j} S_ij (i > j); Aqk = S^qk_ij e^{g_i-g_j} (j <= i)
+//      (I + A)^-1 by blocks (fla/ops/utils/solve_tril.py:184-331): the four
+//        16x16 diagonal inverses by forward substitution in fp32, then the merge
+//        on tcgen05 in tf32 (K-major operands) with the transposed factors
+//          M = Lo^T D^T,  E = D^T (I - M),  X^T = E (I + M^2)
+//        (D: the diagonal-block inverses, Lo: the off-diagonal blocks of A;
+//        (I + A) = (I + Ld)(I + D Lo) and (I + M)^-1 = (I - M)(I + M^2), M^4 = 0)
+//      w = Ai (beta e^g k) and u^T = (beta v)^T Ai^T on tcgen05  (fla/ops/gated_delta_rule/wy_fast.py:27-81)
+//    and writes per (chunk, head) blobs that are already the shared-memory images
+//    the state pass multiplies from: W, U^T, Aqk (bf16, 128-byte swizzled) and the
+//    gate factors e^{g_t}, e^{g_last - g_t}, e^{g_last}.
+// 2. gdn_state_tc_kernel -- one CTA per (sequence x head, 128-wide V slice[, segment]),
+//    sequential over chunks, in the transposed frame (rows of h^T = V columns of
+//    the state live in the 128 TMEM lanes and in the registers of 128 threads):
+//      P    = h^T W^T           (tcgen05, M128 N64 K128)
+//      v_new = u - P; vg = v_new e^{g_last - g_t}   (threads, fp32)
+//      X    = vg^T K            (tcgen05, M128 N128 K64); h <- e^{g_last} h + X
+//                                                  (fla/ops/common/chunk_delta_h.py:52-224)
+//      O    = scale (e^{g_i} h^T Q^T + v_new^T Aqk^T)   (tcgen05, two M128 N64 products)
+//                                                  (fla/ops/common/chunk_o.py:41-128)
+//    The output is formed in the same pass from the state at the chunk start, so
+//    no per-chunk state snapshot is written or read back.  Warps 0-3 run the
+//    dependent chain, warps 4-7 drain the output products, warp 8 issues the
+//    MMAs and warp 9 streams the next chunks' blobs and q/k tiles.
+//
+// Numerics follow the reference's rounding points: normalised q/k, Ai, w, u,
+// v_new, the gated v_new and the state operand are bf16; S, A, the solve (tf32
+// operands), gates, the state and every accumulation are fp32.
+//
+// Every mbarrier wait is bounded.  A wait that gives up records its site in the
+// workspace error word; the CTA stops issuing work, waits (bounded) for the
+// copies and MMAs it already issued, and frees TMEM only if those completed.
+#include "common.cuh"
+#include "kb200_internal.h"
+#include "tc_common.cuh"
+#include "gdn_tc.cuh"
+#include <algorithm>
+#include <cstdlib>
+
+namespace kb {
+namespace gdntc {
+
+using bf16 = __nv_bfloat16;
+constexpr int BT = 64;
+
+// Byte offset of 16-byte chunk `ch` (0..7) of row `row` inside a 128-byte-swizzled
+// atom (the atom base is 1024-aligned; rows are 128 bytes).
+KB_DEVI uint32_t swz(int row, int ch) { return (uint32_t)(row * 128 + ((ch ^ (row & 7)) << 4)); }
+
+// Round a dynamic shared-memory pointer up to 1024 bytes by pointer arithmetic on
+// the shared array itself, so the compiler keeps knowing it is shared memory (and
+// emits shared, not generic, loads and stores).
+KB_DEVI unsigned char* align1024(unsigned char* p) {
+  return p + ((1024u - (smem_u32(p) & 1023u)) & 1023u);
+}
+
+// Bounded wait of this file: about 0.2 s at B200 clocks, far above any normal wait
+// (microseconds), so a lost arrival ends the CTA quickly instead of holding the GPU.
+constexpr long long WAIT_BUDGET = 400000000LL;
+KB_DEVI bool wait_(uint64_t* bar, uint32_t parity) { return tc::mbar_wait(bar, parity, WAIT_BUDGET); }
+
+KB_DEVI void fail(int* err, int code) {
+  if (err) atomicCAS(err, 0, code);
+}
+
+struct ChunkLoc { int n, it, bos, len; };
+KB_DEVI ChunkLoc locate(const TcParams& p, int c) {
+  ChunkLoc r;
+  if (p.cu_seqlens) {
+    r.n = p.chunk_indices[2 * c];
+    r.it = p.chunk_indices[2 * c + 1];
+    if (r.n < 0) { r.n = r.it = r.bos = r.len = 0; return r; }
+    const int s = p.cu_seqlens[r.n], e = p.cu_seqlens[r.n + 1];
+    r.bos = s;
+    r.len = min(BT, e - s - r.it * BT);
+  } else {
+    r.n = c / p.NT;
+    r.it = c % p.NT;
+    r.bos = r.n * p.T;
+    r.len = min(BT, p.T - r.it * BT);
+  }
+  return r;
+}
+
+// Timing probes of the debug build (-DKB_GDN_TRACE): clock64() at phase boundaries
+// of one CTA of each kernel, written to a buffer set by kb200_gdn_set_trace.
+#ifdef KB_GDN_TRACE
+__device__ long long* g_gdn_trace;
+#define PTRACE(slot) do { if (g_gdn_trace && blockIdx.x == 200 && blockIdx.y == 0 && threadIdx.x == 0) \
+  g_gdn_trace[(slot)] = clock64(); } while (0)
+#define STRACE(li, slot) do { if (g_gdn_trace && blockIdx.x == 0 && blockIdx.y == 0 && (li) < 256) \
+  g_gdn_trace[64 + (li) * 8 + (slot)] = clock64(); } while (0)
+#else
+#define PTRACE(slot) do { } while (0)
+#define STRACE(li, slot) do { } while (0)
+#endif
+
+KB_DEVI float bf(uint32_t u, int hi) { return hi ? __uint_as_float(u & 0xffff0000u) : __uint_as_float(u << 16); }
+
+// ===========================================================================
+// 1. Prep.  Grid (chunk slots, H); 128 threads.  Row work (one TMEM lane of an
+// M = 64 product per thread) is done by lanes 0-15 of each warp: row r = 16 w + l,
+// which is where an M = 64 tcgen05 product puts row r (lane 32 (r / 16) + r % 16).
+// ===========================================================================
+template <int V>
+struct PrepLayout {
+  static constexpr uint32_t KT = 0;            // k tile, then beta e^g k      [2 atoms][64][128 B]
+  static constexpr uint32_t QT = 16384;        // q tile; later T1 (Lo^T, E) and the bf16 Ai^T tile
+  static constexpr uint32_t T2 = 32768;        // D^T (fp32)
+  static constexpr uint32_t T3 = 49152;        // M (fp32, A operand)
+  static constexpr uint32_t T4 = 65536;        // B operands of the merge (fp32, K-major): D, then M^T, then (M^2)^T
+  static constexpr uint32_t VT = 81920;        // v tile, then beta v           [V/64 atoms][64][128 B]
+  static constexpr uint32_t DIAG = VT + V * 128;   // fp32 [64][17]: the diagonal 16x16 blocks of A
+  static constexpr uint32_t MISC = DIAG + 64 * 17 * 4;
+  static constexpr uint32_t BYTES = MISC + 640 + 1024;
+  static constexpr uint32_t TMEM_COLS = (128 + V / 2) <= 256 ? 256 : 512;
+};
+
+struct PrepMisc {
+  float gcs[64];
+  float bs[64];
+  uint64_t tma_bar, mma_bar;
+  uint32_t tmem_base;
+  int abort;
+};
+
+template <int V>
+__global__ void __launch_bounds__(128, 2) gdn_prep_tc_kernel(const __grid_constant__ PrepMaps maps, TcParams p) {
+  using LY = PrepLayout<V>;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* sm = align1024(smem_raw);
+  PrepMisc& ms = *reinterpret_cast<PrepMisc*>(sm + LY::MISC);
+  float* diag = reinterpret_cast<float*>(sm + LY::DIAG);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int c = blockIdx.x, h = blockIdx.y, H = p.H;
+  const ChunkLoc loc = locate(p, c);
+  const int t0 = loc.bos + loc.it * BT, L = loc.len;
+  if (L <= 0) return;
+  if (*reinterpret_cast<volatile int*>(p.err)) return;   // an earlier CTA already gave up
+  if (tid == 0) {
+    tc::mbar_init(&ms.tma_bar, 1);
+    tc::mbar_init(&ms.mma_bar, 1);
+    ms.abort = 0;
+    tc::fence_barrier_init();
+  }
+  if (warp == 0) {
+    tc::tmem_alloc(&ms.tmem_base, LY::TMEM_COLS);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  PTRACE(0);
+  tc::tc_fence_after();
+  const uint32_t tmem = ms.tmem_base;
+  const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);    // this warp's TMEM lane quarter
+  const bool rowt = lane < 16;
+  const int r = warp * 16 + lane;                                // row of an M = 64 product
+  int mma_uses = 0;                                              // commits on mma_bar so far
+  bool ok = true;
+
+  if (tid == 0) {
+    tc::mbar_expect_tx(&ms.tma_bar, (uint32_t)(4 + V / 64) * 8192u);
+#pragma unroll
+    for (int a = 0; a < 2; ++a) {
+      tc::tma_load_3d(sm + LY::KT + a * 8192, &maps.k, &ms.tma_bar, a * 64, h, t0);
+      tc::tma_load_3d(sm + LY::QT + a * 8192, &maps.q, &ms.tma_bar, a * 64, h, t0);
+    }
+#pragma unroll
+    for (int a = 0; a < V / 64; ++a) tc::tma_load_3d(sm + LY::VT + a * 8192, &maps.v, &ms.tma_bar, a * 64, h, t0);
+  }
+  // gate cumsum (warp 0) and beta (warp 1) while the tiles land
+  if (warp == 0) {
+    const int i0 = 2 * lane, i1 = i0 + 1;
+    const float g0 = (i0 < L) ? p.g[(size_t)(t0 + i0) * H + h] : 0.f;
+    const float g1 = (i1 < L) ? p.g[(size_t)(t0 + i1) * H + h] : 0.f;
+    const float pair = g0 + g1;
+    float incl = pair;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    const float excl = incl - pair;
+    ms.gcs[i0] = excl + g0;
+    ms.gcs[i1] = excl + g0 + g1;
+  } else if (warp == 1) {
+    for (int i = lane; i < BT; i += 32) ms.bs[i] = (i < L) ? __bfloat162float(p.beta[(size_t)(t0 + i) * H + h]) : 0.f;
+  }
+  ok = wait_(&ms.tma_bar, 0);
+  if (!__syncthreads_and(ok)) {
+    if (tid == 0) {
+      fail(p.err, 41);
+      wait_(&ms.tma_bar, 0);   // let the copies land before the CTA exits
+    }
+    ok = false;
+  }
+  // gate factors of the chunk for the state pass: e^{g_t}, e^{g_last - g_t} (0 past the
+  // chunk end, so those rows drop out of the state update) and e^{g_last}
+  if (ok && tid < 64) {
+    float* gb = p.gb + ((size_t)c * H + h) * G_FLOATS;
+    const float gl = ms.gcs[L - 1], gt = ms.gcs[tid];
+    gb[tid] = tid < L ? __expf(gt) : 0.f;
+    gb[64 + tid] = tid < L ? __expf(gl - gt) : 0.f;
+    if (tid == 0) {
+      gb[128] = __expf(gl);
+      gb[129] = gb[130] = gb[131] = 0.f;
+    }
+  }
+  // optional L2 norm of the q and k rows (y = x / sqrt(sum x^2 + 1e-6), bf16), in
+  // place in shared memory and to the normalised global copies the state pass reads
+  if (ok && p.l2norm) {
+    const int rr = tid & 63;
+    unsigned char* tile = sm + (tid < 64 ? LY::KT : LY::QT);
+    bf16* dst = tid < 64 ? p.kn : p.qn;
+    uint4 x[16];
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      x[j] = *reinterpret_cast<const uint4*>(tile + (j >> 3) * 8192 + swz(rr, j & 7));
+      const uint32_t* w = reinterpret_cast<const uint32_t*>(&x[j]);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float a = bf(w[e], 0), b = bf(w[e], 1);
+        ss = fmaf(a, a, fmaf(b, b, ss));
+      }
+    }
+    const float rs = 1.0f / sqrtf(ss + 1e-6f);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      uint32_t* w = reinterpret_cast<uint32_t*>(&x[j]);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) w[e] = pack_bf16(bf(w[e], 0) * rs, bf(w[e], 1) * rs);
+      *reinterpret_cast<uint4*>(tile + (j >> 3) * 8192 + swz(rr, j & 7)) = x[j];
+      if (rr < L) *reinterpret_cast<uint4*>(dst + ((size_t)(t0 + rr) * H + h) * 128 + j * 8) = x[j];
+    }
+  }
+  tc::fence_proxy_async_smem();
+  __syncthreads();
+  PTRACE(1);
+  // ---- S_kk = K K^T (TMEM cols 0..63), S_qk = Q K^T (cols 64..127) ----
+  if (ok && tid == 0) {
+    tc::tc_fence_after();
+    constexpr uint32_t ID = tc::idesc_f32acc(1, 64, 64, 0, 0);
+    const uint64_t dk = tc::sdesc_sw128_kmajor(sm + LY::KT), dq = tc::sdesc_sw128_kmajor(sm + LY::QT);
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      const uint32_t off = ((ks >> 2) * 8192 + (ks & 3) * 32) >> 4;
+      tc::mma_bf16(tmem + 0, dk + off, dk + off, ID, ks > 0);
+      tc::mma_bf16(tmem + 64, dq + off, dk + off, ID, ks > 0);
+    }
+    tc::tc_commit(&ms.mma_bar);
+  }
+  if (ok) ++mma_uses;
+  // wait for the MMA round just committed: every thread waits, the verdict is shared
+  auto mma_wait = [&]() {
+    bool w = wait_(&ms.mma_bar, (mma_uses - 1) & 1);
+    tc::tc_fence_after();
+    if (!__syncthreads_and(w)) {
+      if (tid == 0) fail(p.err, 42);
+      ok = false;
+    }
+  };
+  if (ok) mma_wait();
+  // ---- per row: Aqk row -> global blob; diagonal block of A -> smem; Lo^T row -> T1 ----
+  if (ok) {
+    uint32_t s[64];
+    tc::tmem_ld32(tl + 0, s);
+    tc::tmem_ld32(tl + 32, s + 32);
+    tc::tmem_wait_ld();
+    const float gr = ms.gcs[r], br = ms.bs[r];
+    const bool rv = rowt && r < L;
+    const int blk = warp;   // = r / 16
+    if (rowt) {
+      // diagonal 16x16 block of A, strictly lower: A_rj = beta_r e^{g_r - g_j} S_rj
+#pragma unroll
+      for (int kb = 0; kb < 4; ++kb) {
+        if (kb != blk) continue;
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) {
+          const int j = kb * 16 + jj;
+          diag[r * 17 + jj] = (rv && j < r) ? br * __expf(gr - ms.gcs[j]) * __uint_as_float(s[j]) : 0.f;
+        }
+      }
+      // column r of A below the diagonal blocks (A_kr = beta_k e^{g_k - g_r} S_rk, S
+      // symmetric) is row r of Lo^T
+      unsigned char* t1 = sm + LY::QT;
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        float v4[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int k = 4 * q + e;
+          v4[e] = (rv && k < L && (k >> 4) > blk) ? ms.bs[k] * __expf(ms.gcs[k] - gr) * __uint_as_float(s[k]) : 0.f;
+        }
+        *reinterpret_cast<float4*>(t1 + (q >> 3) * 8192 + swz(r, q & 7)) = make_float4(v4[0], v4[1], v4[2], v4[3]);
+      }
+    }
+    tc::tmem_ld32(tl + 64, s);
+    tc::tmem_ld32(tl + 96, s + 32);
+    tc::tmem_wait_ld();
+    if (rowt) {
+      // Aqk row r: (q_r . k_j) e^{g_r - g_j} for j <= r (chunk_o.py:100-112), bf16
+      unsigned char* ab = reinterpret_cast<unsigned char*>(p.ab) + ((size_t)c * H + h) * AQK_BYTES;
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int j0 = ch * 8 + 2 * e;
+          const float a0 = (rv && j0 <= r) ? __uint_as_float(s[j0]) * __expf(gr - ms.gcs[j0]) : 0.f;
+          const float a1 = (rv && j0 + 1 <= r) ? __uint_as_float(s[j0 + 1]) * __expf(gr - ms.gcs[j0 + 1]) : 0.f;
+          w[e] = pack_bf16(a0, a1);
+        }
+        *reinterpret_cast<uint4*>(ab + swz(r, ch)) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+  }
+  tc::fence_proxy_async_smem();
+  tc::tc_fence_before();
+  __syncthreads();
+  PTRACE(2);
+  // ---- D^T row r: column r % 16 of the inverse of (I + diagonal block r / 16), by
+  // forward substitution (fp32); kept in registers for E ----
+  // element (row n, column r) of a fp32 tile [2 atoms of 32 columns][64 rows][128 B]
+  auto st_col = [&](uint32_t off, int n, float val) {
+    *reinterpret_cast<float*>(sm + off + (r >> 5) * 8192 + n * 128 + ((((r & 31) >> 2) ^ (n & 7)) << 4) + (r & 3) * 4) = val;
+  };
+  float x[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) x[i] = 0.f;
+  if (ok && rowt) {
+    const int cc = lane;
+    const float* dg = diag + warp * 16 * 17;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) x[i] = (i == cc) ? 1.f : 0.f;
+#pragma unroll
+    for (int rr = 1; rr < 16; ++rr) {
+      float acc = 0.f;
+#pragma unroll
+      for (int j = 0; j < rr; ++j) acc = fmaf(dg[rr * 17 + j], x[j], acc);
+      if (rr > cc) x[rr] = -acc;
+    }
+    unsigned char* t2 = sm + LY::T2;
+#pragma unroll
+    for (int q = 0; q < 16; ++q) {
+      float4 v4 = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int kb = 0; kb < 4; ++kb)
+        if (kb == warp && (q >> 2) == kb)
+          v4 = make_float4(x[4 * (q & 3)], x[4 * (q & 3) + 1], x[4 * (q & 3) + 2], x[4 * (q & 3) + 3]);
+      *reinterpret_cast<float4*>(t2 + (q >> 3) * 8192 + swz(r, q & 7)) = v4;
+    }
+    // the same values as column r of D: the K-major B operand of round 1
+#pragma unroll
+    for (int n = 0; n < 64; ++n) {
+      float val = 0.f;
+#pragma unroll
+      for (int kb = 0; kb < 4; ++kb)
+        if (kb == warp && (n >> 4) == kb) val = x[n & 15];
+      st_col(LY::T4, n, val);
+    }
+  }
+  tc::fence_proxy_async_smem();
+  __syncthreads();
+  PTRACE(3);
+  constexpr uint32_t ID_TF = tc::idesc_f32acc(2, 64, 64, 0, 0);   // tf32, both K-major
+  // C[cols] = A B^T-tile (M64 N64 K64, tf32): A rows [m][k], B rows [n][k], fp32, K-major
+  auto tf32_product = [&](uint32_t col, uint32_t a_off, uint32_t b_off) {
+    const uint64_t da = tc::sdesc_sw128_kmajor(sm + a_off), db = tc::sdesc_sw128_kmajor(sm + b_off);
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      const uint32_t off = ((ks >> 2) * 8192 + (ks & 3) * 32) >> 4;
+      tc::mma_tf32(tmem + col, da + off, db + off, ID_TF, ks > 0);
+    }
+  };
+  // ---- round 1: M = Lo^T D^T -> cols 128..191 (B rows: D) ----
+  if (ok && tid == 0) {
+    tc::tc_fence_after();
+    tf32_product(128, LY::QT, LY::T4);
+    tc::tc_commit(&ms.mma_bar);
+  }
+  if (ok) { ++mma_uses; mma_wait(); PTRACE(30 + mma_uses); }
+  // row r of a fp32 M = 64 product (TMEM cols col..col+63) -> registers
+  auto ld_row64 = [&](uint32_t col, float* dst) {
+    uint32_t u[64];
+    tc::tmem_ld32(tl + col, u);
+    tc::tmem_ld32(tl + col + 32, u + 32);
+    tc::tmem_wait_ld();
+#pragma unroll
+    for (int i = 0; i < 64; ++i) dst[i] = __uint_as_float(u[i]);
+  };
+  auto st_row64 = [&](uint32_t off, const float* v) {
+    if (!rowt) return;
+#pragma unroll
+    for (int q = 0; q < 16; ++q)
+      *reinterpret_cast<float4*>(sm + off + (q >> 3) * 8192 + swz(r, q & 7)) =
+          make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+  };
+  // row r of a product transposed into column r of a K-major B tile
+  auto st_colT = [&](uint32_t off, const float* v) {
+    if (!rowt) return;
+#pragma unroll
+    for (int n = 0; n < 64; ++n) st_col(off, n, v[n]);
+  };
+  float e[64];
+  if (ok) {
+    ld_row64(128, e);
+    st_row64(LY::T3, e);
+    st_colT(LY::T4, e);
+  }
+  tc::fence_proxy_async_smem();
+  tc::tc_fence_before();
+  __syncthreads();
+  PTRACE(4);
+  // ---- round 2: M^2 = M M -> cols 192..255, Q = D^T M -> cols 128..191 (B rows: M^T) ----
+  if (ok && tid == 0) {
+    tc::tc_fence_after();
+    tf32_product(192, LY::T3, LY::T4);
+    tf32_product(128, LY::T2, LY::T4);
+    tc::tc_commit(&ms.mma_bar);
+  }
+  if (ok) { ++mma_uses; mma_wait(); PTRACE(30 + mma_uses); }
+  if (ok) {
+    // E = D^T - Q (row r), kept in registers; M^2 -> T3
+    ld_row64(128, e);
+#pragma unroll
+    for (int kb = 0; kb < 4; ++kb) {
+      if (kb == warp) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) e[kb * 16 + i] = x[i] - e[kb * 16 + i];
+#pragma unroll
+        for (int i = 0; i < 64; ++i)
+          if ((i >> 4) != kb) e[i] = -e[i];
+      }
+    }
+    st_row64(LY::QT, e);
+    float m2[64];
+    ld_row64(192, m2);
+    st_colT(LY::T4, m2);
+  }
+  tc::fence_proxy_async_smem();
+  tc::tc_fence_before();
+  __syncthreads();
+  PTRACE(5);
+  // ---- round 3: F = E M^2 -> cols 128..191 (B rows: (M^2)^T) ----
+  if (ok && tid == 0) {
+    tc::tc_fence_after();
+    tf32_product(128, LY::QT, LY::T4);
+    tc::tc_commit(&ms.mma_bar);
+  }
+  if (ok) { ++mma_uses; mma_wait(); PTRACE(30 + mma_uses); }
+  if (ok) {
+    // (I + A)^-1 transposed: row r = E_r + F_r, bf16 -> the Ai^T tile (one 64-column atom at QT)
+    float f[64];
+    ld_row64(128, f);
+    if (rowt) {
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        uint32_t w[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) w[q] = pack_bf16(e[8 * ch + 2 * q] + f[8 * ch + 2 * q], e[8 * ch + 2 * q + 1] + f[8 * ch + 2 * q + 1]);
+        *reinterpret_cast<uint4*>(sm + LY::QT + swz(r, ch)) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+    // k rows -> bf16(bf16(k beta) e^g) (wy_fast.py:77-79), v rows -> bf16(v beta) (:67), in place
+    {
+      const int rr = tid & 63, a = tid >> 6;
+      const float b = ms.bs[rr], eg = __expf(ms.gcs[rr]);
+      unsigned char* row = sm + LY::KT + a * 8192;
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        uint4 v4 = *reinterpret_cast<const uint4*>(row + swz(rr, ch));
+        uint32_t* w = reinterpret_cast<uint32_t*>(&v4);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          w[q] = pack_bf16(bf16_round(bf(w[q], 0) * b) * eg, bf16_round(bf(w[q], 1) * b) * eg);
+        *reinterpret_cast<uint4*>(row + swz(rr, ch)) = v4;
+      }
+    }
+    for (int job = tid; job < 64 * (V / 64); job += 128) {
+      const int rr = job & 63, a = job >> 6;
+      const float b = ms.bs[rr];
+      unsigned char* row = sm + LY::VT + a * 8192;
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        uint4 v4 = *reinterpret_cast<const uint4*>(row + swz(rr, ch));
+        uint32_t* w = reinterpret_cast<uint32_t*>(&v4);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) w[q] = pack_bf16(bf(w[q], 0) * b, bf(w[q], 1) * b);
+        *reinterpret_cast<uint4*>(row + swz(rr, ch)) = v4;
+      }
+    }
+  }
+  tc::fence_proxy_async_smem();
+  tc::tc_fence_before();
+  __syncthreads();
+  PTRACE(6);
+  // ---- w = Ai (beta e^g k) -> cols 0..127 (M64 N128); u^T = (beta v)^T Ai^T -> cols
+  // 128 + 64 s (M128 N64 per 128-wide V slice s).  Ai^T rows are Ai's MN-major image. ----
+  if (ok && tid == 0) {
+    tc::tc_fence_after();
+    constexpr uint32_t ID_W = tc::idesc_f32acc(1, 64, 128, 1, 1);
+    constexpr uint32_t ID_U = tc::idesc_f32acc(1, 128, 64, 1, 1);
+    const uint64_t dai = tc::sdesc_sw128_mnmajor(sm + LY::QT, 8192);
+    const uint64_t dkt = tc::sdesc_sw128_mnmajor(sm + LY::KT, 8192);
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) tc::mma_bf16(tmem + 0, dai + ks * 128, dkt + ks * 128, ID_W, ks > 0);
+#pragma unroll
+    for (int vs = 0; vs < V / 128; ++vs) {
+      const uint64_t dv = tc::sdesc_sw128_mnmajor(sm + LY::VT + vs * 16384, 8192);
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) tc::mma_bf16(tmem + 128 + 64 * vs, dv + ks * 128, dai + ks * 128, ID_U, ks > 0);
+    }
+    tc::tc_commit(&ms.mma_bar);
+  }
+  if (ok) { ++mma_uses; mma_wait(); PTRACE(30 + mma_uses); }
+  if (ok) {
+    // w row r -> W blob (bf16, [2 atoms][64 rows][128 B] swizzled); the TMEM loads are
+    // warp-collective, only the row lanes store
+    unsigned char* wb = reinterpret_cast<unsigned char*>(p.wb) + ((size_t)c * H + h) * W_BYTES;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      uint32_t u[64];
+      tc::tmem_ld32(tl + 64 * half, u);
+      tc::tmem_ld32(tl + 64 * half + 32, u + 32);
+      tc::tmem_wait_ld();
+      if (rowt) {
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch) {
+          uint4 o;
+          o.x = pack_bf16(__uint_as_float(u[8 * ch]), __uint_as_float(u[8 * ch + 1]));
+          o.y = pack_bf16(__uint_as_float(u[8 * ch + 2]), __uint_as_float(u[8 * ch + 3]));
+          o.z = pack_bf16(__uint_as_float(u[8 * ch + 4]), __uint_as_float(u[8 * ch + 5]));
+          o.w = pack_bf16(__uint_as_float(u[8 * ch + 6]), __uint_as_float(u[8 * ch + 7]));
+          *reinterpret_cast<uint4*>(wb + half * 8192 + swz(r, ch)) = o;
+        }
+      }
+    }
+    // u^T row v = tid (M = 128: all lanes) -> U^T blob ([V rows][64 tokens] bf16 swizzled)
+    unsigned char* ub = reinterpret_cast<unsigned char*>(p.ub) + ((size_t)c * H + h) * (size_t)(V * 128);
+#pragma unroll
+    for (int vs = 0; vs < V / 128; ++vs) {
+      uint32_t u[64];
+      tc::tmem_ld32(tl + 128 + 64 * vs, u);
+      tc::tmem_ld32(tl + 128 + 64 * vs + 32, u + 32);
+      tc::tmem_wait_ld();
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        uint4 o;
+        o.x = pack_bf16(__uint_as_float(u[8 * ch]), __uint_as_float(u[8 * ch + 1]));
+        o.y = pack_bf16(__uint_as_float(u[8 * ch + 2]), __uint_as_float(u[8 * ch + 3]));
+        o.z = pack_bf16(__uint_as_float(u[8 * ch + 4]), __uint_as_float(u[8 * ch + 5]));
+        o.w = pack_bf16(__uint_as_float(u[8 * ch + 6]), __uint_as_float(u[8 * ch + 7]));
+        *reinterpret_cast<uint4*>(ub + vs * 16384 + swz(tid, ch)) = o;
+      }
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  PTRACE(7);
+  bool keep = false;
+  if (!ok && mma_uses > 0 && tid == 0) {
+    // a wait gave up with MMAs issued: one more (bounded) wait for their completion
+    // before TMEM may be freed
+    keep = !wait_(&ms.mma_bar, (mma_uses - 1) & 1);
+    ms.abort = keep;
+  }
+  __syncthreads();
+  PTRACE(8);
+  if (warp == 0 && !ms.abort) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, LY::TMEM_COLS);
+  }
+}
+
+// ===========================================================================
+// 2. State pass with the output fused.  Grid (V/128 [+ 1 transition CTA in the
+// segment-local pass], N*H*nseg); three warpgroups: state (thread v owns row v of
+// h^T: its V column of the state, 128 fp32 registers), output, and control (one
+// thread issues every MMA, one streams the loads).  The state threads hand each
+// operand to the issuer through an mbarrier (h_ready, vg_ready) and wait for the
+// products on the commits (p_full, x_full), so the chain never waits on MMA issue.
+// ===========================================================================
+struct StLayout {
+  static constexpr uint32_t W = 0, Q = 16384, K = 32768, U = 49152, A = 65536;
+  static constexpr uint32_t STAGE = 73728;                     // 72 KB, 1024-aligned
+  static constexpr uint32_t H = 2 * STAGE;                     // bf16 h^T  [2 atoms][128 rows][128 B]
+  static constexpr uint32_t VG = H + 32768;                    // bf16 gated v_new^T [128 rows][64 tokens]
+  static constexpr uint32_t VN = VG + 16384;                   // bf16 v_new^T
+  static constexpr uint32_t OST = VN + 16384;                  // bf16 output tile [2 atoms][64 tokens][128 B] (TMA store)
+  static constexpr uint32_t MISC = OST + 16384;
+  static constexpr uint32_t BYTES = MISC + 2048 + 1024;        // = the 227 KB a CTA may use
+};
+static_assert(StLayout::STAGE % 1024 == 0 && StLayout::H % 1024 == 0 && StLayout::OST % 1024 == 0,
+              "tiles must be 1024-aligned");
+static_assert(StLayout::BYTES <= 232448, "shared memory of one CTA");
+
+struct StMisc {
+  float g[2][G_FLOATS];            // gate factors of the chunk in each stage (bulk-copied with the stage)
+  float eg[4][64];                 // e^{g_i} of chunk li in slot li & 3, for the output warps
+  uint64_t in_full[2], in_empty[2], p_full, x_full, o_full[2], o_free[2], h_ready, vg_ready, drain;
+  uint32_t tmem_base;
+  int abort;
+  int keep_tmem;
+};
+
+// The output tile of one chunk into the staging tile: thread v (TMEM lane v) writes
+// o[t][v] = scale (e^{g_t} O_inter[v][t] + O_intra[v][t]) for the 64 tokens t
+// (bf16, [2 atoms][64 tokens][128 B], 128-byte swizzle) and releases the O buffer
+// once both halves are in registers.  One copy of the code (not inlined), so the
+// state loop stays small in the instruction cache.
+__device__ __noinline__ void emit_stage(unsigned char* __restrict__ ost_base, uint32_t t_oi, uint32_t t_oa,
+                                        const float* __restrict__ eg_s, float scale, int v, uint64_t* o_free) {
+  // e^{g_t} for the 64 tokens, into registers before any store
+  float eg[64];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float4 t = reinterpret_cast<const float4*>(eg_s)[i];
+    eg[4 * i] = t.x; eg[4 * i + 1] = t.y; eg[4 * i + 2] = t.z; eg[4 * i + 3] = t.w;
+  }
+  // lanes v (even) and v + 1 pair up: per token pair (2u, 2u + 1) the even lane
+  // writes token 2u and the odd lane token 2u + 1, each as one 32-bit word holding
+  // columns (v & ~1, v | 1)
+  const bool odd = v & 1;
+  const uint32_t row0 = smem_u32(ost_base) + (v >> 6) * 8192 + (v & 6) * 2;
+  const int vc = (v & 63) >> 3;
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    uint32_t oi[32], oa[32];
+    tc::tmem_ld32(t_oi + 32 * half, oi);
+    tc::tmem_ld32(t_oa + 32 * half, oa);
+    tc::tmem_wait_ld();
+    if (half == 1) {
+      tc::tc_fence_before();
+      tc::mbar_arrive(o_free);
+    }
+#pragma unroll
+    for (int u = 0; u < 16; ++u) {
+      const int ta = 32 * half + 2 * u, tb = ta + 1;
+      const float ya = scale * fmaf(eg[ta], __uint_as_float(oi[2 * u]), __uint_as_float(oa[2 * u]));
+      const float yb = scale * fmaf(eg[tb], __uint_as_float(oi[2 * u + 1]), __uint_as_float(oa[2 * u + 1]));
+      // even lane keeps token ta and receives the odd lane's ta; odd lane the reverse
+      const float mine = odd ? ya : yb;
+      const float other = __shfl_xor_sync(0xffffffffu, mine, 1);
+      const int tt = odd ? tb : ta;
+      const uint32_t w = odd ? pack_bf16(other, yb) : pack_bf16(ya, other);
+      asm volatile("st.shared.b32 [%0], %1;\n" ::"r"(row0 + tt * 128 + ((vc ^ (tt & 7)) << 4)), "r"(w) : "memory");
+    }
+  }
+}
+
+// TMEM columns of the state pass
+constexpr uint32_t XCOL = 0, PCOL = 128, OICOL = 192, OACOL = 256;   // O buffers at +128 b
+
+// Warps 0-3: the state chain; warps 4-7: the output of each chunk; warp 8: MMA
+// issuer; warp 9: loads.  (Twelve warps leave a thread 168 registers: the state
+// row takes 128 of them, so the chain reads TMEM 32 columns at a time.)
+constexpr int ST_THREADS = 384;
+
+template <int V>
+__global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_tc_kernel(const __grid_constant__ StMaps maps, TcParams p) {
+  using LY = StLayout;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* sm = align1024(smem_raw);
+  StMisc& ms = *reinterpret_cast<StMisc*>(sm + LY::MISC);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, H = p.H;
+  const int nseg = p.seg_mode ? p.nseg : 1;
+  const int nh = blockIdx.y / nseg, seg = blockIdx.y % nseg, n = nh / H, h = nh % H;
+  const bool trans = p.seg_mode == 1 && (int)blockIdx.x >= V / 128;
+  const int v0 = trans ? 0 : blockIdx.x * 128;
+  if (p.seg_mode == 1 && (seg == nseg - 1 || (trans && seg == 0))) return;
+  if (*reinterpret_cast<volatile int*>(p.err)) return;   // an earlier kernel or CTA already gave up
+  int bos, Tn, cbase;
+  if (p.cu_seqlens) {
+    bos = p.cu_seqlens[n];
+    Tn = p.cu_seqlens[n + 1] - bos;
+    cbase = p.chunk_offsets[n];
+  } else {
+    bos = n * p.T;
+    Tn = p.T;
+    cbase = n * p.NT;
+  }
+  const int NTn = (Tn + BT - 1) / BT;
+  const int it0 = p.seg_mode ? seg * p.seg_chunks : 0;
+  const int it1 = p.seg_mode ? min(NTn, it0 + p.seg_chunks) : NTn;
+  const int nl = max(0, it1 - it0);
+  const bool out = p.seg_mode != 1;           // this pass writes o
+  const bool load_u = !trans;                 // the transition runs with u = 0
+  if (tid == 0) {
+    for (int s = 0; s < 2; ++s) {
+      tc::mbar_init(&ms.in_full[s], 1);
+      tc::mbar_init(&ms.in_empty[s], 1);
+      tc::mbar_init(&ms.o_full[s], 1);
+      tc::mbar_init(&ms.o_free[s], 128);
+    }
+    tc::mbar_init(&ms.p_full, 1);
+    tc::mbar_init(&ms.x_full, 1);
+    tc::mbar_init(&ms.h_ready, 128);
+    tc::mbar_init(&ms.vg_ready, 128);
+    tc::mbar_init(&ms.drain, 1);
+    ms.abort = 0;
+    ms.keep_tmem = 0;
+    tc::fence_barrier_init();
+  }
+  if (warp == 0) {
+    tc::tmem_alloc(&ms.tmem_base, 512);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = ms.tmem_base;
+  auto aborted = [&]() { return *((volatile int*)&ms.abort) != 0; };
+
+  if (warp >= 8) {
+    if (warp == 8 && lane == 0) {
+      // ---------------------------------------------------------------- MMA issuer
+      constexpr uint32_t ID_P = tc::idesc_f32acc(1, 128, 64, 0, 0);
+      constexpr uint32_t ID_X = tc::idesc_f32acc(1, 128, 128, 0, 1);
+      const uint64_t dh = tc::sdesc_sw128_kmajor(sm + LY::H);
+      const uint64_t dvg = tc::sdesc_sw128_kmajor(sm + LY::VG), dvn = tc::sdesc_sw128_kmajor(sm + LY::VN);
+      bool ok = true;
+      for (int li = 0; li < nl && ok; ++li) {
+        const int s = li & 1, b = li & 1;
+        unsigned char* st = sm + s * LY::STAGE;
+        // P = h^T W^T and O_inter = h^T Q^T once the state threads wrote h^T
+        ok = wait_(&ms.in_full[s], (li >> 1) & 1) && wait_(&ms.h_ready, li & 1) &&
+             (!out || li < 2 || wait_(&ms.o_free[b], ((li >> 1) - 1) & 1)) && !aborted();
+        if (!ok) { fail(p.err, 81); break; }
+        tc::tc_fence_after();
+        const uint64_t dw = tc::sdesc_sw128_kmajor(st + LY::W);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          tc::mma_bf16(tmem + PCOL, dh + (((ks >> 2) * 16384 + (ks & 3) * 32) >> 4),
+                       dw + (((ks >> 2) * 8192 + (ks & 3) * 32) >> 4), ID_P, ks > 0);
+        tc::tc_commit(&ms.p_full);
+        if (out) {
+          const uint64_t dq = tc::sdesc_sw128_kmajor(st + LY::Q);
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks)
+            tc::mma_bf16(tmem + OICOL + 128 * b, dh + (((ks >> 2) * 16384 + (ks & 3) * 32) >> 4),
+                         dq + (((ks >> 2) * 8192 + (ks & 3) * 32) >> 4), ID_P, ks > 0);
+        }
+        // X = vg^T K (the state update) and O_intra = v_new^T Aqk^T once vg, v_new are written
+        ok = wait_(&ms.vg_ready, li & 1) && !aborted();
+        if (!ok) { fail(p.err, 82); break; }
+        tc::tc_fence_after();
+        const uint64_t dk = tc::sdesc_sw128_mnmajor(st + LY::K, 8192);
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) tc::mma_bf16(tmem + XCOL, dvg + ks * 2, dk + ks * 128, ID_X, ks > 0);
+        tc::tc_commit(&ms.x_full);
+        if (out) {
+          const uint64_t da = tc::sdesc_sw128_kmajor(st + LY::A);
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) tc::mma_bf16(tmem + OACOL + 128 * b, dvn + ks * 2, da + ks * 2, ID_P, ks > 0);
+          tc::tc_commit(&ms.o_full[b]);
+        }
+        tc::tc_commit(&ms.in_empty[s]);
+        STRACE(li, 5);
+      }
+      if (!ok) ms.abort = 1;
+      // every MMA issued here completes before TMEM is freed
+      tc::tc_commit(&ms.drain);
+      if (!wait_(&ms.drain, 0)) { fail(p.err, 72); ms.keep_tmem = 1; }
+    } else if (warp == 9 && lane == 0) {
+      // ---------------------------------------------------------------- loads
+      const uint32_t bytes = W_BYTES + 16384u + G_BYTES + (load_u ? 16384u : 0u) + (out ? 16384u + AQK_BYTES : 0u);
+      int issued = 0;
+      for (int li = 0; li < nl; ++li) {
+        const int s = li & 1;
+        if (li >= 2 && !wait_(&ms.in_empty[s], ((li >> 1) - 1) & 1)) {
+          if (!aborted()) fail(p.err, 51);
+          ms.abort = 1;
+          break;
+        }
+        if (aborted()) break;
+        const int it = it0 + li;
+        const size_t ch = (size_t)(cbase + it) * H + h;
+        const int t0 = bos + it * BT;
+        unsigned char* st = sm + s * LY::STAGE;
+        tc::mbar_expect_tx(&ms.in_full[s], bytes);
+        tc::bulk_load(st + LY::W, reinterpret_cast<const unsigned char*>(p.wb) + ch * W_BYTES, W_BYTES, &ms.in_full[s]);
+        tc::bulk_load(ms.g[s], p.gb + ch * G_FLOATS, G_BYTES, &ms.in_full[s]);
+        tc::tma_load_3d(st + LY::K, &maps.k, &ms.in_full[s], 0, h, t0);
+        tc::tma_load_3d(st + LY::K + 8192, &maps.k, &ms.in_full[s], 64, h, t0);
+        if (load_u)
+          tc::bulk_load(st + LY::U, reinterpret_cast<const unsigned char*>(p.ub) + ch * (size_t)(V * 128) + v0 * 128,
+                        16384, &ms.in_full[s]);
+        if (out) {
+          tc::tma_load_3d(st + LY::Q, &maps.q, &ms.in_full[s], 0, h, t0);
+          tc::tma_load_3d(st + LY::Q + 8192, &maps.q, &ms.in_full[s], 64, h, t0);
+          tc::bulk_load(st + LY::A, reinterpret_cast<const unsigned char*>(p.ab) + ch * AQK_BYTES, AQK_BYTES,
+                        &ms.in_full[s]);
+        }
+        ++issued;
+      }
+      // every load issued here lands before the CTA may exit
+      bool drained = true;
+      for (int li = max(0, issued - 2); li < issued; ++li) drained &= wait_(&ms.in_full[li & 1], (li >> 1) & 1);
+      if (!drained) { fail(p.err, 52); ms.keep_tmem = 1; }
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------------ output
+    if (out) {
+      const int v = tid - 128;
+      const uint32_t tl = tmem + ((uint32_t)((warp - 4) * 32) << 16);
+      // output of chunk lo: o = scale (e^{g_i} O_inter + O_intra), bf16, token rows of
+      // this V slice
+    const float scale = p.scale;
+    const size_t ostride = (size_t)H * V;
+    auto emit = [&](int lo) {
+      const int b = lo & 1;
+      const int it = it0 + lo, L = min(BT, Tn - it * BT);
+      const int t0 = bos + it * BT;
+      // the previous chunk's TMA store must have finished reading the staging tile
+      if (tid == 128) tc::bulk_wait_group_read0();
+      tc::bar_sync_named(2, 128);
+      if (tid == 128) STRACE(lo, 1);
+      emit_stage(sm + LY::OST, tl + OICOL + 128 * b, tl + OACOL + 128 * b, ms.eg[lo & 3], scale, v, &ms.o_free[b]);
+      if (tid == 128) STRACE(lo, 7);
+      tc::fence_proxy_async_smem();
+      tc::bar_sync_named(2, 128);
+      if (L == BT) {
+        if (tid == 128) {
+          tc::tma_store_3d(&maps.o, sm + LY::OST, v0, h, t0);
+          tc::tma_store_3d(&maps.o, sm + LY::OST + 8192, v0 + 64, h, t0);
+          tc::bulk_commit_group();
+        }
+      } else {
+        // the last, partial chunk of a sequence: only its L rows, as 16-byte vectors
+        for (int j = v; j < L * 16; j += 128) {
+          const int t = j >> 4, c = j & 15;
+          *reinterpret_cast<uint4*>(p.o + (size_t)(t0 + t) * ostride + (size_t)h * V + v0 + c * 8) =
+              *reinterpret_cast<const uint4*>(sm + LY::OST + (c >> 3) * 8192 + swz(t, c & 7));
+        }
+      }
+    };
+      for (int lo = 0; lo < nl; ++lo) {
+        const bool w = wait_(&ms.o_full[lo & 1], (lo >> 1) & 1);
+        if (!__all_sync(0xffffffffu, w)) {
+          if (lane == 0) fail(p.err, 61);
+          ms.abort = 1;
+          break;
+        }
+        tc::tc_fence_after();
+        emit(lo);
+      }
+      if (tid == 128) tc::bulk_wait_group0();   // the output stores complete before the CTA exits
+    }
+  } else {
+    // ------------------------------------------------------------------ state chain
+    const int v = tid;
+    const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
+    float hr[128];
+    const bool seg_start0 = p.seg_mode != 0 && seg > 0;
+#pragma unroll
+    for (int k = 0; k < 128; ++k) {
+      float init;
+      if (trans)
+        init = (k == v) ? 1.f : 0.f;
+      else if (seg_start0)
+        init = p.seg_mode == 2 ? p.seg_h[(((size_t)nh * nseg + seg) * 128 + k) * V + v0 + v] : 0.f;
+      else
+        init = p.h0 ? p.h0[((size_t)nh * 128 + k) * V + v0 + v] : 0.f;
+      hr[k] = init;
+    }
+    float dec = 1.f;
+    bool ok = true;
+    // h <- e^{g_last} h + X (the last chunk's state update), 64 columns per TMEM wait
+    auto update_h = [&]() {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint32_t xr[32];
+        tc::tmem_ld32(tl + XCOL + 32 * q, xr);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) hr[32 * q + i] = fmaf(dec, hr[32 * q + i], __uint_as_float(xr[i]));
+      }
+    };
+    for (int li = 0; li < nl; ++li) {
+      const int s = li & 1;
+      unsigned char* st = sm + s * LY::STAGE;
+      if (tid == 0) STRACE(li, 0);
+      // (a) the previous chunk's update, then the bf16 h^T operand
+      if (li > 0) {
+        ok = wait_(&ms.x_full, (li - 1) & 1);
+        if (!__all_sync(0xffffffffu, ok) || aborted()) { ok = false; break; }
+        tc::tc_fence_after();
+        update_h();
+      }
+#pragma unroll
+      for (int c16 = 0; c16 < 16; ++c16) {
+        uint4 o;
+        o.x = pack_bf16(hr[8 * c16], hr[8 * c16 + 1]);
+        o.y = pack_bf16(hr[8 * c16 + 2], hr[8 * c16 + 3]);
+        o.z = pack_bf16(hr[8 * c16 + 4], hr[8 * c16 + 5]);
+        o.w = pack_bf16(hr[8 * c16 + 6], hr[8 * c16 + 7]);
+        *reinterpret_cast<uint4*>(sm + LY::H + (c16 >> 3) * 16384 + swz(v, c16 & 7)) = o;
+      }
+      tc::fence_proxy_async_smem();
+      tc::tc_fence_before();
+      tc::mbar_arrive(&ms.h_ready);
+      if (tid == 0) STRACE(li, 2);
+      // (b) v_new = u - h^T w^T (chunk_delta_h.py:142-163), gated by e^{g_last - g_t}
+      ok = wait_(&ms.p_full, li & 1) && wait_(&ms.in_full[s], (li >> 1) & 1);
+      if (!__all_sync(0xffffffffu, ok) || aborted()) { ok = false; break; }
+      tc::tc_fence_after();
+      if (tid == 0) STRACE(li, 3);
+      const float* G = ms.g[s];
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+      uint32_t pr[32];
+      tc::tmem_ld32(tl + PCOL + 32 * half, pr);
+      tc::tmem_wait_ld();
+#pragma unroll
+      for (int ch = 4 * half; ch < 4 * half + 4; ++ch) {
+        uint4 u4 = make_uint4(0, 0, 0, 0);
+        if (load_u) u4 = *reinterpret_cast<const uint4*>(st + LY::U + swz(v, ch));
+        const float4 f0 = reinterpret_cast<const float4*>(G + 64)[2 * ch];
+        const float4 f1 = reinterpret_cast<const float4*>(G + 64)[2 * ch + 1];
+        const float fg[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
+        const uint32_t uw[4] = {u4.x, u4.y, u4.z, u4.w};
+        uint32_t vnw[4], vgw[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float a0 = bf(uw[q], 0) - __uint_as_float(pr[8 * (ch & 3) + 2 * q]);
+          const float a1 = bf(uw[q], 1) - __uint_as_float(pr[8 * (ch & 3) + 2 * q + 1]);
+          vnw[q] = pack_bf16(a0, a1);
+          vgw[q] = pack_bf16(a0 * fg[2 * q], a1 * fg[2 * q + 1]);
+        }
+        *reinterpret_cast<uint4*>(sm + LY::VN + swz(v, ch)) = make_uint4(vnw[0], vnw[1], vnw[2], vnw[3]);
+        *reinterpret_cast<uint4*>(sm + LY::VG + swz(v, ch)) = make_uint4(vgw[0], vgw[1], vgw[2], vgw[3]);
+      }
+      }
+      dec = G[128];
+      if (out && v < 64) ms.eg[li & 3][v] = G[v];
+      tc::fence_proxy_async_smem();
+      tc::tc_fence_before();
+      tc::mbar_arrive(&ms.vg_ready);
+      if (tid == 0) STRACE(li, 4);
+    }
+    if (ok && nl > 0) {
+      ok = wait_(&ms.x_full, (nl - 1) & 1);
+      tc::tc_fence_after();
+      update_h();
+    }
+    ok = tc::bar_red_and(1, 128, ok && !aborted());
+    if (!ok) {
+      if (tid == 0) fail(p.err, 71);
+      ms.abort = 1;
+    } else {
+      float* dst = nullptr;
+      if (p.seg_mode == 1)
+        dst = trans ? p.seg_m + ((size_t)nh * nseg + seg) * 128 * 128 : p.seg_b + ((size_t)nh * nseg + seg) * 128 * V;
+      else if (p.ht && (p.seg_mode == 0 || seg == nseg - 1))
+        dst = p.ht + (size_t)nh * 128 * V;
+      if (dst) {
+        if (trans) {
+          // row v of the transposed transition (column v of M)
+#pragma unroll
+          for (int k = 0; k < 128; k += 4)
+            *reinterpret_cast<float4*>(dst + (size_t)v * 128 + k) = make_float4(hr[k], hr[k + 1], hr[k + 2], hr[k + 3]);
+        } else {
+#pragma unroll
+          for (int k = 0; k < 128; ++k) dst[(size_t)k * V + v0 + v] = hr[k];
+        }
+      }
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 0 && !ms.keep_tmem) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace gdntc
+}  // namespace kb
+
+#ifdef KB_GDN_TRACE
+extern "C" int kb200_gdn_set_trace(long long* p) {
+  return cudaMemcpyToSymbol(kb::gdntc::g_gdn_trace, &p, sizeof(p)) == cudaSuccess ? 0 : 4;
+}
+#endif
+
+// ===========================================================================
+// Host side
+// ===========================================================================
+namespace {
+using namespace kb::gdntc;
+
+int map3d(CUtensorMap* m, const void* base, int64_t tokens, int64_t H, int D) {
+  kb::tc::EncodeTiledFn fn = kb::tc::encode_tiled_fn();
+  if (!fn) return kb::set_error(KB200_ERR_LAUNCH, "gdn_tc: cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)(tokens > 0 ? tokens : 1)};
+  cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)H * D * 2};
+  cuuint32_t box[3] = {64, 1, (cuuint32_t)BT};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return kb::set_error(KB200_ERR_LAUNCH, "gdn_tc: tensor map encode failed (%d)", (int)r);
+  return KB200_OK;
+}
+
+int sm_count_tc() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+template <int V>
+int launch_v(const KB200GdnArgs* a, const kb::gdntc::TcWs& L, char* ws, cudaStream_t st) {
+  TcParams p{};
+  p.q = (const __nv_bfloat16*)a->q;
+  p.k = (const __nv_bfloat16*)a->k;
+  p.v = (const __nv_bfloat16*)a->v;
+  p.g = a->g;
+  p.beta = (const __nv_bfloat16*)a->beta;
+  p.h0 = a->initial_state;
+  p.o = (__nv_bfloat16*)a->o;
+  p.ht = a->final_state;
+  p.cu_seqlens = a->cu_seqlens;
+  p.chunk_indices = a->chunk_indices;
+  p.chunk_offsets = a->chunk_offsets;
+  p.qn = a->use_qk_l2norm ? (__nv_bfloat16*)(ws + L.qn) : nullptr;
+  p.kn = a->use_qk_l2norm ? (__nv_bfloat16*)(ws + L.kn) : nullptr;
+  p.wb = ws + L.wb;
+  p.ab = ws + L.ab;
+  p.ub = ws + L.ub;
+  p.gb = (float*)(ws + L.gb);
+  p.T = (int)a->T;
+  p.H = (int)a->H;
+  p.V = V;
+  p.NT = (int)((a->T + BT - 1) / BT);
+  p.scale = a->scale;
+  p.l2norm = a->use_qk_l2norm;
+  p.err = (int*)(ws + L.err);
+  p.seg_b = (float*)(ws + L.seg_b);
+  p.seg_m = (float*)(ws + L.seg_m);
+  p.seg_h = (float*)(ws + L.seg_h);
+  const int H = (int)a->H;
+  const int64_t tokens = a->B * a->T;
+  if (cudaMemsetAsync(p.err, 0, sizeof(int), st) != cudaSuccess) return kb::check_launch("gdn error word reset");
+  const int nchunks = (int)a->num_chunks;
+  if (nchunks > 0) {
+    PrepMaps pm;
+    if (int e = map3d(&pm.q, a->q, tokens, H, 128)) return e;
+    if (int e = map3d(&pm.k, a->k, tokens, H, 128)) return e;
+    if (int e = map3d(&pm.v, a->v, tokens, H, V)) return e;
+    const size_t s1 = PrepLayout<V>::BYTES;
+    cudaFuncSetAttribute(gdn_prep_tc_kernel<V>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s1);
+    gdn_prep_tc_kernel<V><<<dim3(nchunks, H), 128, s1, st>>>(pm, p);
+    if (int e = kb::check_launch("gdn_prep_tc_kernel")) return e;
+  }
+  StMaps sm;
+  const void* qsrc = a->use_qk_l2norm ? (const void*)p.qn : a->q;
+  const void* ksrc = a->use_qk_l2norm ? (const void*)p.kn : a->k;
+  if (int e = map3d(&sm.q, qsrc, tokens, H, 128)) return e;
+  if (int e = map3d(&sm.k, ksrc, tokens, H, 128)) return e;
+  if (int e = map3d(&sm.o, a->o, tokens, H, V)) return e;
+  const size_t s2 = StLayout::BYTES;
+  cudaFuncSetAttribute(gdn_state_tc_kernel<V>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s2);
+  const unsigned nh = (unsigned)(a->N * H);
+  if (L.nseg < 2) {
+    p.seg_mode = 0;
+    gdn_state_tc_kernel<V><<<dim3(V / 128, nh), ST_THREADS, s2, st>>>(sm, p);
+    return kb::check_launch("gdn_state_tc_kernel");
+  }
+  p.nseg = L.nseg;
+  p.seg_chunks = L.seg_chunks;
+  p.seg_mode = 1;
+  gdn_state_tc_kernel<V><<<dim3(V / 128 + 1, nh * L.nseg), ST_THREADS, s2, st>>>(sm, p);
+  if (int e = kb::check_launch("gdn_state_tc_kernel (segment-local)")) return e;
+  if (int e = kb::gdn_seg_combine(p.seg_b, p.seg_m, p.seg_h, L.nseg, (int)nh, 128, V, p.err, st)) return e;
+  p.seg_mode = 2;
+  gdn_state_tc_kernel<V><<<dim3(V / 128, nh * L.nseg), ST_THREADS, s2, st>>>(sm, p);
+  return kb::check_launch("gdn_state_tc_kernel");
+}
+}  // namespace
+
+namespace kb {
+namespace gdntc {
+
+bool supported(const KB200GdnArgs* a) { return a->K == 128 && (a->V == 128 || a->V == 256 || a->V == 512); }
+
+// Segments of the state pass: the final pass holds one CTA per (sequence x head,
+// V slice, segment) and should fill the SMs; every segment keeps >= 16 chunks.
+void plan(const KB200GdnArgs* a, int* nseg, int* seg_chunks) {
+  *nseg = 1;
+  *seg_chunks = 0;
+  if (a->cu_seqlens) return;
+  const long nt = (a->T + BT - 1) / BT;
+  const long ctas = (long)a->N * a->H * (a->V / 128);
+  long cap = std::max(1L, (long)sm_count_tc() / ctas);
+  if (const char* e = getenv("KB200_GDN_SEGMENTS")) cap = std::max(1, atoi(e));
+  long ns = std::min(std::min(cap, nt / 16), 32L);
+  if (ns > 1) {
+    *seg_chunks = (int)((nt + ns - 1) / ns);
+    *nseg = (int)((nt + *seg_chunks - 1) / *seg_chunks);
+  }
+  if (*nseg < 2) { *nseg = 1; *seg_chunks = 0; }
+}
+
+TcWs layout(const KB200GdnArgs* a) {
+  const size_t TT = (size_t)a->B * a->T, H = a->H, V = a->V, C = (size_t)a->num_chunks;
+  TcWs L{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) { size_t o = off; off = align_up(off + bytes); return o; };
+  L.err = take(16);
+  const size_t nqk = a->use_qk_l2norm ? TT * H * 128 * 2 : 0;
+  L.qn = take(nqk);
+  L.kn = take(nqk);
+  L.wb = take(C * H * W_BYTES);
+  L.ab = take(C * H * AQK_BYTES);
+  L.ub = take(C * H * V * 128);
+  L.gb = take(C * H * G_BYTES);
+  plan(a, &L.nseg, &L.seg_chunks);
+  const size_t segs = L.nseg > 1 ? (size_t)a->N * H * L.nseg : 0;
+  L.seg_b = take(segs * 128 * V * 4);
+  L.seg_m = take(segs * 128 * 128 * 4);
+  L.seg_h = take(segs * 128 * V * 4);
+  L.total = off;
+  return L;
+}
+
+int launch_count(const KB200GdnArgs* a) {
+  int ns, sc;
+  plan(a, &ns, &sc);
+  return (a->num_chunks > 0 ? 1 : 0) + (ns > 1 ? 3 : 1);
+}
+
+int launch(const KB200GdnArgs* a, const TcWs& L, char* ws, cudaStream_t st) {
+  if (a->V == 128) return launch_v<128>(a, L, ws, st);
+  if (a->V == 256) return launch_v<256>(a, L, ws, st);
+  if (a->V == 512) return launch_v<512>(a, L, ws, st);
+  return set_error(KB200_ERR_INVALID, "gdn_tc: unsupported V");
+}
+
+}  // namespace gdntc
+}  // namespace kb

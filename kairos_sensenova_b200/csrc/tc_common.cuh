@@ -63,6 +63,15 @@ KB_DEVI void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar
       ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
+// Tiled TMA store shared -> global (bulk-group completion), and its group waits.
+KB_DEVI void tma_store_3d(const CUtensorMap* map, const void* src, int x, int y, int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];\n"
+               ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+KB_DEVI void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;\n" ::: "memory"); }
+KB_DEVI void bulk_wait_group_read0() { asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory"); }
+KB_DEVI void bulk_wait_group0() { asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory"); }
 KB_DEVI void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -95,6 +104,12 @@ KB_DEVI void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t 
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
       " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n"
+      ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+KB_DEVI void mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n"
       ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
 }
 // A operand from TMEM (rows = lanes, K packed along 32-bit columns), B from shared memory.
@@ -140,6 +155,17 @@ KB_DEVI void tmem_st32(uint32_t taddr, const uint32_t* r) {
         "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
         "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31]));
 }
+// 32 lanes x 8 consecutive 32-bit columns (load).
+KB_DEVI void tmem_ld8(uint32_t taddr, uint32_t* r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+// Warpgroup register reallocation (all four warps of a warpgroup execute it).
+template <int N>
+KB_DEVI void setmaxnreg_inc() { asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(N)); }
+template <int N>
+KB_DEVI void setmaxnreg_dec() { asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(N)); }
 KB_DEVI void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
 KB_DEVI void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
 
@@ -155,6 +181,43 @@ KB_DEVI uint64_t sdesc_sw128_kmajor(const void* smem) {
   d |= (uint64_t)1 << 46;                // descriptor version (sm_100)
   d |= (uint64_t)2 << 61;                // layout: SWIZZLE_128B
   return d;
+}
+
+// Shared-memory matrix descriptor: MN-major operand, 128-byte swizzle.  Each 128-byte
+// row holds 128 bytes of consecutive M (or N) elements at one K index; K rows are
+// 128 bytes apart, so 8-row K groups are 1024 bytes apart (SBO); the next 128-byte
+// block of M/N elements starts `mn_atom_stride` bytes further (LBO).  Tile base
+// 1024-aligned.  Advancing by k K-rows adds (k * 128) >> 4 to the address field.
+KB_DEVI uint64_t sdesc_sw128_mnmajor(const void* smem, uint32_t mn_atom_stride) {
+  const uint64_t addr = smem_u32(smem);
+  uint64_t d = 0;
+  d |= (addr >> 4) & 0x3FFFull;
+  d |= (uint64_t)((mn_atom_stride >> 4) & 0x3FFF) << 16;   // LBO: next block along M/N
+  d |= (uint64_t)(1024 >> 4) << 32;                       // SBO: next 8-row K group
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+// General instruction descriptor with f32 accumulation: fmt 0 f16 / 1 bf16 / 2 tf32
+// (kind::f16 or kind::tf32), a_mn / b_mn select MN-major operands.
+__host__ __device__ constexpr uint32_t idesc_f32acc(int fmt, int M, int N, int a_mn, int b_mn) {
+  return (1u << 4) | ((uint32_t)fmt << 7) | ((uint32_t)fmt << 10) | ((uint32_t)a_mn << 15) |
+         ((uint32_t)b_mn << 16) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// Named barrier over `count` threads that also ANDs a predicate across them.
+KB_DEVI bool bar_red_and(int id, int count, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, %2, %3, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id), "r"(count)
+      : "memory");
+  return r != 0;
+}
+KB_DEVI void bar_sync_named(int id, int count) {
+  asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(count) : "memory");
 }
 
 // Instruction descriptor, kind::f8f6f4: A = B = e4m3, D = f32, both K-major.

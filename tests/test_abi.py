@@ -39,9 +39,13 @@ def test_gdn_workspace_size_and_validation():
     L = _lib.lib()
     a = _args()
     n = L.kb200_gdn_workspace_size(ctypes.byref(a))
-    # gc + w + u + v_new + h snapshots + normalised q,k
-    TT, H, K, V = 100, 2, 128, 128
-    assert n >= TT * H * (4 + 2 * K * 2 + 2 * K + 2 * V * 2) + 2 * H * K * V * 2
+    # K = 128 (tcgen05 path): per (chunk, head) the W (16 KB), U^T (V*128 B), Aqk (8 KB)
+    # and gate-factor (528 B) blobs, plus the normalised q, k copies
+    TT, H, K, V, C = 100, 2, 128, 128, 2
+    assert n >= C * H * (16384 + V * 128 + 8192 + 528) + 2 * TT * H * K * 2
+    # K = 256 (mma.sync path): gc + w + u + v_new + h snapshots + normalised q,k
+    n256 = L.kb200_gdn_workspace_size(ctypes.byref(_args(K=256)))
+    assert n256 >= TT * H * (4 + 2 * 256 * 2 + 2 * 256 + 2 * V * 2) + 2 * H * 256 * V * 2
     for bad in (dict(K=96), dict(V=64), dict(num_chunks=3), dict(B=0)):
         assert L.kb200_gdn_workspace_size(ctypes.byref(_args(**bad))) == 0
     rc = L.kb200_gdn_chunk_fwd(ctypes.byref(_args(K=96)), None, 0, None)
@@ -67,23 +71,27 @@ def test_python_op_rejects_cpu_and_grad():
 
 
 def test_gdn_state_plan_launch_count(monkeypatch):
-    """The state-pass plan is host logic: 32-wide V slices and one segment for
-    many heads, 16-wide slices and concurrent segments (5 launches) for one
-    8-GPU rank's 3 heads, no segments for short or variable-length input.
-    (Without a GPU the plan assumes B200's 148 SMs.)"""
+    """The state-pass plan is host logic.  K = 128 (tcgen05 kernels): one prep launch,
+    then one state launch, or three (segment-local pass, combine, final pass) when
+    one CTA per (sequence x head, V slice) leaves SMs idle and every segment keeps
+    >= 16 chunks; no segments for short or variable-length input.  K = 256 (mma.sync
+    kernels): 3 launches, 5 with segments.  (Without a GPU the plan assumes B200's
+    148 SMs.)"""
     L = _lib.lib()
     monkeypatch.delenv('KB200_GDN_SEGMENTS', raising=False)
     monkeypatch.delenv('KB200_GDN_STATE_BV', raising=False)
     cnt = lambda **kw: L.kb200_gdn_launch_count(ctypes.byref(_args(**kw)))  # noqa: E731
     nt = lambda T: (T + 63) // 64  # noqa: E731
-    assert cnt(T=32760, H=24, num_chunks=nt(32760)) == 3
-    assert cnt(T=32760, H=3, num_chunks=nt(32760)) == 5
-    assert cnt(T=200, H=3, num_chunks=nt(200)) == 3
+    assert cnt(T=32760, H=24, num_chunks=nt(32760)) == 4
+    assert cnt(T=32760, H=3, num_chunks=nt(32760)) == 4
+    assert cnt(T=32760, H=160, num_chunks=nt(32760)) == 2     # the heads alone fill the SMs
+    assert cnt(T=200, H=3, num_chunks=nt(200)) == 2
     assert cnt(T=0, H=3, num_chunks=0) == 1           # no chunks: the state pass only (h0 -> ht)
     assert cnt(K=96) == -1
+    assert cnt(K=256, V=256, T=32760, H=3, num_chunks=nt(32760)) == 5
     seg = L.kb200_gdn_workspace_size(ctypes.byref(_args(T=32760, H=3, num_chunks=nt(32760))))
     monkeypatch.setenv('KB200_GDN_SEGMENTS', '1')
-    assert cnt(T=32760, H=3, num_chunks=nt(32760)) == 3
+    assert cnt(T=32760, H=3, num_chunks=nt(32760)) == 2
     one = L.kb200_gdn_workspace_size(ctypes.byref(_args(T=32760, H=3, num_chunks=nt(32760))))
     # segments add the local end states, transitions and start states (fp32)
     assert seg - one >= 3 * 6 * (128 * 128 * 4) * 3
