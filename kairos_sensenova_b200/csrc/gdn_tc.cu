@@ -108,20 +108,20 @@ __device__ long long* g_gdn_trace;
 KB_DEVI float bf(uint32_t u, int hi) { return hi ? __uint_as_float(u & 0xffff0000u) : __uint_as_float(u << 16); }
 
 // ===========================================================================
-// 1. Prep.  Grid (chunk slots, H); 128 threads.  Row work (one TMEM lane of an
-// M = 64 product per thread) is done by lanes 0-15 of each warp: row r = 16 w + l,
-// which is where an M = 64 tcgen05 product puts row r (lane 32 (r / 16) + r % 16).
+// 1. Prep.  Grid (chunk slots, H); 128 threads.  An M = 64 tcgen05 product puts
+// row r in TMEM lane 32 (r / 16) + r % 16; each warp reads its 16 rows with the
+// two-half load, so thread (warp w, lane l) owns row r = 16 w + l % 16 and the
+// 32-column half l / 16 of it: all 128 threads work on every phase.
 // ===========================================================================
 template <int V>
 struct PrepLayout {
   static constexpr uint32_t KT = 0;            // k tile, then beta e^g k      [2 atoms][64][128 B]
-  static constexpr uint32_t QT = 16384;        // q tile; later T1 (Lo^T, E) and the bf16 Ai^T tile
-  static constexpr uint32_t T2 = 32768;        // D^T (fp32)
-  static constexpr uint32_t T3 = 49152;        // M (fp32, A operand)
-  static constexpr uint32_t T4 = 65536;        // B operands of the merge (fp32, K-major): D, then M^T, then (M^2)^T
+  static constexpr uint32_t QT = 16384;        // q tile; then T1: Lo^T, E (fp32); then the bf16 Ai^T tile
+  static constexpr uint32_t T2 = 32768;        // D^T rows (fp32)
+  static constexpr uint32_t T3 = 49152;        // A (fp32 [64][64], column-swizzled), then M rows
+  static constexpr uint32_t T4 = 65536;        // D rows, then M^T rows, then (M^2)^T rows (fp32)
   static constexpr uint32_t VT = 81920;        // v tile, then beta v           [V/64 atoms][64][128 B]
-  static constexpr uint32_t DIAG = VT + V * 128;   // fp32 [64][17]: the diagonal 16x16 blocks of A
-  static constexpr uint32_t MISC = DIAG + 64 * 17 * 4;
+  static constexpr uint32_t MISC = VT + V * 128;
   static constexpr uint32_t BYTES = MISC + 640 + 1024;
   static constexpr uint32_t TMEM_COLS = (128 + V / 2) <= 256 ? 256 : 512;
 };
@@ -134,13 +134,33 @@ struct PrepMisc {
   int abort;
 };
 
+// A scratch: element (r, j) of a [64][64] fp32 array at r * 64 + (j ^ (r & 31)), so
+// that both a row and a column are read without bank conflicts.
+KB_DEVI int as_idx(int r, int j) { return r * 64 + (j ^ (r & 31)); }
+
+// 8 consecutive fp32 of row `row`, columns 8c..8c+7 (c in 0..7), of a fp32 K-major
+// tile [2 atoms of 32 columns][64 rows][128 B] -> two 16-byte chunks.
+KB_DEVI void st_f32x8(unsigned char* tile, int row, int c, const float* x) {
+  unsigned char* base = tile + (c >> 2) * 8192;
+  const int ch = (c & 3) * 2;
+  *reinterpret_cast<float4*>(base + swz(row, ch)) = make_float4(x[0], x[1], x[2], x[3]);
+  *reinterpret_cast<float4*>(base + swz(row, ch + 1)) = make_float4(x[4], x[5], x[6], x[7]);
+}
+KB_DEVI void ld_f32x8(const unsigned char* tile, int row, int c, float* x) {
+  const unsigned char* base = tile + (c >> 2) * 8192;
+  const int ch = (c & 3) * 2;
+  const float4 a = *reinterpret_cast<const float4*>(base + swz(row, ch));
+  const float4 b = *reinterpret_cast<const float4*>(base + swz(row, ch + 1));
+  x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+}
+
 template <int V>
 __global__ void __launch_bounds__(128, 2) gdn_prep_tc_kernel(const __grid_constant__ PrepMaps maps, TcParams p) {
   using LY = PrepLayout<V>;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = align1024(smem_raw);
   PrepMisc& ms = *reinterpret_cast<PrepMisc*>(sm + LY::MISC);
-  float* diag = reinterpret_cast<float*>(sm + LY::DIAG);
+  float* As = reinterpret_cast<float*>(sm + LY::T3);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int c = blockIdx.x, h = blockIdx.y, H = p.H;
   const ChunkLoc loc = locate(p, c);
@@ -162,10 +182,11 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_tc_kernel(const __grid_consta
   PTRACE(0);
   tc::tc_fence_after();
   const uint32_t tmem = ms.tmem_base;
-  const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);    // this warp's TMEM lane quarter
-  const bool rowt = lane < 16;
-  const int r = warp * 16 + lane;                                // row of an M = 64 product
-  int mma_uses = 0;                                              // commits on mma_bar so far
+  const uint32_t tq = tmem + ((uint32_t)(warp * 32) << 16);     // this warp's TMEM lane quarter
+  const int r = warp * 16 + (lane & 15);                          // row of M = 64 products
+  const int hc = lane >> 4;                                       // column half
+  const int blk = warp;                                           // r / 16
+  int mma_uses = 0;
   bool ok = true;
 
   if (tid == 0) {
@@ -204,6 +225,7 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_tc_kernel(const __grid_consta
     }
     ok = false;
   }
+  PTRACE(1);
   // gate factors of the chunk for the state pass: e^{g_t}, e^{g_last - g_t} (0 past the
   // chunk end, so those rows drop out of the state update) and e^{g_last}
   if (ok && tid < 64) {
@@ -246,7 +268,6 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_tc_kernel(const __grid_consta
   }
   tc::fence_proxy_async_smem();
   __syncthreads();
-  PTRACE(1);
   // ---- S_kk = K K^T (TMEM cols 0..63), S_qk = Q K^T (cols 64..127) ----
   if (ok && tid == 0) {
     tc::tc_fence_after();
@@ -260,9 +281,8 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_tc_kernel(const __grid_consta
     }
     tc::tc_commit(&ms.mma_bar);
   }
-  if (ok) ++mma_uses;
-  // wait for the MMA round just committed: every thread waits, the verdict is shared
   auto mma_wait = [&]() {
+    ++mma_uses;
     bool w = wait_(&ms.mma_bar, (mma_uses - 1) & 1);
     tc::tc_fence_after();
     if (!__syncthreads_and(w)) {
@@ -271,110 +291,89 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_tc_kernel(const __grid_consta
     }
   };
   if (ok) mma_wait();
-  // ---- per row: Aqk row -> global blob; diagonal block of A -> smem; Lo^T row -> T1 ----
-  if (ok) {
-    uint32_t s[64];
-    tc::tmem_ld32(tl + 0, s);
-    tc::tmem_ld32(tl + 32, s + 32);
-    tc::tmem_wait_ld();
-    const float gr = ms.gcs[r], br = ms.bs[r];
-    const bool rv = rowt && r < L;
-    const int blk = warp;   // = r / 16
-    if (rowt) {
-      // diagonal 16x16 block of A, strictly lower: A_rj = beta_r e^{g_r - g_j} S_rj
-#pragma unroll
-      for (int kb = 0; kb < 4; ++kb) {
-        if (kb != blk) continue;
-#pragma unroll
-        for (int jj = 0; jj < 16; ++jj) {
-          const int j = kb * 16 + jj;
-          diag[r * 17 + jj] = (rv && j < r) ? br * __expf(gr - ms.gcs[j]) * __uint_as_float(s[j]) : 0.f;
-        }
-      }
-      // column r of A below the diagonal blocks (A_kr = beta_k e^{g_k - g_r} S_rk, S
-      // symmetric) is row r of Lo^T
-      unsigned char* t1 = sm + LY::QT;
-#pragma unroll
-      for (int q = 0; q < 16; ++q) {
-        float v4[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int k = 4 * q + e;
-          v4[e] = (rv && k < L && (k >> 4) > blk) ? ms.bs[k] * __expf(ms.gcs[k] - gr) * __uint_as_float(s[k]) : 0.f;
-        }
-        *reinterpret_cast<float4*>(t1 + (q >> 3) * 8192 + swz(r, q & 7)) = make_float4(v4[0], v4[1], v4[2], v4[3]);
-      }
-    }
-    tc::tmem_ld32(tl + 64, s);
-    tc::tmem_ld32(tl + 96, s + 32);
-    tc::tmem_wait_ld();
-    if (rowt) {
-      // Aqk row r: (q_r . k_j) e^{g_r - g_j} for j <= r (chunk_o.py:100-112), bf16
-      unsigned char* ab = reinterpret_cast<unsigned char*>(p.ab) + ((size_t)c * H + h) * AQK_BYTES;
-#pragma unroll
-      for (int ch = 0; ch < 8; ++ch) {
-        uint32_t w[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int j0 = ch * 8 + 2 * e;
-          const float a0 = (rv && j0 <= r) ? __uint_as_float(s[j0]) * __expf(gr - ms.gcs[j0]) : 0.f;
-          const float a1 = (rv && j0 + 1 <= r) ? __uint_as_float(s[j0 + 1]) * __expf(gr - ms.gcs[j0 + 1]) : 0.f;
-          w[e] = pack_bf16(a0, a1);
-        }
-        *reinterpret_cast<uint4*>(ab + swz(r, ch)) = make_uint4(w[0], w[1], w[2], w[3]);
-      }
-    }
-  }
-  tc::fence_proxy_async_smem();
-  tc::tc_fence_before();
-  __syncthreads();
   PTRACE(2);
-  // ---- D^T row r: column r % 16 of the inverse of (I + diagonal block r / 16), by
-  // forward substitution (fp32); kept in registers for E ----
-  // element (row n, column r) of a fp32 tile [2 atoms of 32 columns][64 rows][128 B]
-  auto st_col = [&](uint32_t off, int n, float val) {
-    *reinterpret_cast<float*>(sm + off + (r >> 5) * 8192 + n * 128 + ((((r & 31) >> 2) ^ (n & 7)) << 4) + (r & 3) * 4) = val;
-  };
-  float x[16];
+  const float gr = ms.gcs[r], br = ms.bs[r];
+  const bool rv = r < L;
+  // ---- elementwise: Aqk half-row -> global blob; A half-row -> A scratch ----
+  if (ok) {
+    uint32_t sk[32], sq[32];
+    tc::tmem_ld16x32bx2_x32<32>(tq + 0, sk);
+    tc::tmem_ld16x32bx2_x32<32>(tq + 64, sq);
+    tc::tmem_wait_ld();
+    unsigned char* ab = reinterpret_cast<unsigned char*>(p.ab) + ((size_t)c * H + h) * AQK_BYTES;
 #pragma unroll
-  for (int i = 0; i < 16; ++i) x[i] = 0.f;
-  if (ok && rowt) {
-    const int cc = lane;
-    const float* dg = diag + warp * 16 * 17;
+    for (int c8 = 0; c8 < 4; ++c8) {
+      uint32_t w[4];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) x[i] = (i == cc) ? 1.f : 0.f;
+      for (int e = 0; e < 8; e += 2) {
+        float f[2];
 #pragma unroll
-    for (int rr = 1; rr < 16; ++rr) {
-      float acc = 0.f;
-#pragma unroll
-      for (int j = 0; j < rr; ++j) acc = fmaf(dg[rr * 17 + j], x[j], acc);
-      if (rr > cc) x[rr] = -acc;
-    }
-    unsigned char* t2 = sm + LY::T2;
-#pragma unroll
-    for (int q = 0; q < 16; ++q) {
-      float4 v4 = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-      for (int kb = 0; kb < 4; ++kb)
-        if (kb == warp && (q >> 2) == kb)
-          v4 = make_float4(x[4 * (q & 3)], x[4 * (q & 3) + 1], x[4 * (q & 3) + 2], x[4 * (q & 3) + 3]);
-      *reinterpret_cast<float4*>(t2 + (q >> 3) * 8192 + swz(r, q & 7)) = v4;
-    }
-    // the same values as column r of D: the K-major B operand of round 1
-#pragma unroll
-    for (int n = 0; n < 64; ++n) {
-      float val = 0.f;
-#pragma unroll
-      for (int kb = 0; kb < 4; ++kb)
-        if (kb == warp && (n >> 4) == kb) val = x[n & 15];
-      st_col(LY::T4, n, val);
+        for (int q = 0; q < 2; ++q) {
+          const int jj = c8 * 8 + e + q, j = 32 * hc + jj;
+          // e^{g_r - g_j} where the causal masks keep the entry (j <= r)
+          const float fac = (rv && j <= r) ? __expf(gr - ms.gcs[j]) : 0.f;
+          f[q] = __uint_as_float(sq[jj]) * fac;
+          As[as_idx(r, j)] = (j < r) ? br * fac * __uint_as_float(sk[jj]) : 0.f;   // A = beta_r e^{..} S_kk
+        }
+        w[e >> 1] = pack_bf16(f[0], f[1]);
+      }
+      *reinterpret_cast<uint4*>(ab + swz(r, 4 * hc + c8)) = make_uint4(w[0], w[1], w[2], w[3]);
     }
   }
-  tc::fence_proxy_async_smem();
   __syncthreads();
   PTRACE(3);
+  // ---- Lo^T half-row r (column r of A below the diagonal blocks) -> T1; D^T row /
+  // D row of the diagonal-block inverse (forward / back substitution, fp32) ----
+  float x[16];
+  if (ok) {
+    unsigned char* t1 = sm + LY::QT;
+#pragma unroll
+    for (int c8 = 0; c8 < 4; ++c8) {
+      float v8[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int k = 32 * hc + 8 * c8 + e;
+        v8[e] = ((k >> 4) > blk) ? As[as_idx(k, r)] : 0.f;
+      }
+      st_f32x8(t1, r, 4 * hc + c8, v8);
+    }
+    // thread t < 64: column t % 16 of block t / 16's inverse (row t of D^T);
+    // thread t >= 64: row (t - 64) % 16 of it (row t - 64 of D)
+    const int rr = tid & 63, b = rr >> 4, cc = rr & 15;
+    const float* Ab = As;   // A rows 16 b + i, columns 16 b + j
+#pragma unroll
+    for (int i = 0; i < 16; ++i) x[i] = (i == cc) ? 1.f : 0.f;
+    if (tid < 64) {
+#pragma unroll
+      for (int i = 1; i < 16; ++i) {
+        float acc = 0.f;
+#pragma unroll
+        for (int j = 0; j < i; ++j) acc = fmaf(Ab[as_idx(16 * b + i, 16 * b + j)], x[j], acc);
+        if (i > cc) x[i] = -acc;
+      }
+    } else {
+#pragma unroll
+      for (int j = 14; j >= 0; --j) {
+        float acc = 0.f;
+#pragma unroll
+        for (int i = j + 1; i < 16; ++i) acc = fmaf(Ab[as_idx(16 * b + i, 16 * b + j)], x[i], acc);
+        if (j < cc) x[j] = -acc;
+      }
+    }
+    unsigned char* dst = sm + (tid < 64 ? LY::T2 : LY::T4);
+#pragma unroll
+    for (int c8 = 0; c8 < 8; ++c8) {
+      float v8[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v8[e] = ((c8 >> 1) == b) ? x[(c8 & 1) * 8 + e] : 0.f;
+      st_f32x8(dst, rr, c8, v8);
+    }
+  }
+  tc::fence_proxy_async_smem();
+  __syncthreads();
+  PTRACE(4);
   constexpr uint32_t ID_TF = tc::idesc_f32acc(2, 64, 64, 0, 0);   // tf32, both K-major
-  // C[cols] = A B^T-tile (M64 N64 K64, tf32): A rows [m][k], B rows [n][k], fp32, K-major
+  // C[cols] = A B^T (M64 N64 K64, tf32): A rows [m][k], B rows [n][k], fp32, K-major
   auto tf32_product = [&](uint32_t col, uint32_t a_off, uint32_t b_off) {
     const uint64_t da = tc::sdesc_sw128_kmajor(sm + a_off), db = tc::sdesc_sw128_kmajor(sm + b_off);
 #pragma unroll
@@ -383,94 +382,81 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_tc_kernel(const __grid_consta
       tc::mma_tf32(tmem + col, da + off, db + off, ID_TF, ks > 0);
     }
   };
-  // ---- round 1: M = Lo^T D^T -> cols 128..191 (B rows: D) ----
-  if (ok && tid == 0) {
-    tc::tc_fence_after();
-    tf32_product(128, LY::QT, LY::T4);
-    tc::tc_commit(&ms.mma_bar);
-  }
-  if (ok) { ++mma_uses; mma_wait(); PTRACE(30 + mma_uses); }
-  // row r of a fp32 M = 64 product (TMEM cols col..col+63) -> registers
-  auto ld_row64 = [&](uint32_t col, float* dst) {
-    uint32_t u[64];
-    tc::tmem_ld32(tl + col, u);
-    tc::tmem_ld32(tl + col + 32, u + 32);
+  // half-row r of an M = 64 product (TMEM cols col..col+63) -> registers
+  auto ld_half = [&](uint32_t col, float* dst) {
+    uint32_t u[32];
+    tc::tmem_ld16x32bx2_x32<32>(tq + col, u);
     tc::tmem_wait_ld();
 #pragma unroll
-    for (int i = 0; i < 64; ++i) dst[i] = __uint_as_float(u[i]);
+    for (int i = 0; i < 32; ++i) dst[i] = __uint_as_float(u[i]);
   };
-  auto st_row64 = [&](uint32_t off, const float* v) {
-    if (!rowt) return;
+  auto st_half = [&](uint32_t off, const float* v) {
 #pragma unroll
-    for (int q = 0; q < 16; ++q)
-      *reinterpret_cast<float4*>(sm + off + (q >> 3) * 8192 + swz(r, q & 7)) =
-          make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    for (int c8 = 0; c8 < 4; ++c8) st_f32x8(sm + off, r, 4 * hc + c8, v + 8 * c8);
   };
-  // row r of a product transposed into column r of a K-major B tile
-  auto st_colT = [&](uint32_t off, const float* v) {
-    if (!rowt) return;
-#pragma unroll
-    for (int n = 0; n < 64; ++n) st_col(off, n, v[n]);
-  };
-  float e[64];
-  if (ok) {
-    ld_row64(128, e);
-    st_row64(LY::T3, e);
-    st_colT(LY::T4, e);
-  }
-  tc::fence_proxy_async_smem();
-  tc::tc_fence_before();
-  __syncthreads();
-  PTRACE(4);
-  // ---- round 2: M^2 = M M -> cols 192..255, Q = D^T M -> cols 128..191 (B rows: M^T) ----
+  // ---- round 1: M = Lo^T D^T -> cols 128..191, M^T = D Lo -> cols 192..255 ----
   if (ok && tid == 0) {
     tc::tc_fence_after();
-    tf32_product(192, LY::T3, LY::T4);
-    tf32_product(128, LY::T2, LY::T4);
+    tf32_product(128, LY::QT, LY::T4);
+    tf32_product(192, LY::T4, LY::QT);
     tc::tc_commit(&ms.mma_bar);
   }
-  if (ok) { ++mma_uses; mma_wait(); PTRACE(30 + mma_uses); }
+  if (ok) mma_wait();
+  PTRACE(5);
+  float e[32];
   if (ok) {
-    // E = D^T - Q (row r), kept in registers; M^2 -> T3
-    ld_row64(128, e);
-#pragma unroll
-    for (int kb = 0; kb < 4; ++kb) {
-      if (kb == warp) {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) e[kb * 16 + i] = x[i] - e[kb * 16 + i];
-#pragma unroll
-        for (int i = 0; i < 64; ++i)
-          if ((i >> 4) != kb) e[i] = -e[i];
-      }
-    }
-    st_row64(LY::QT, e);
-    float m2[64];
-    ld_row64(192, m2);
-    st_colT(LY::T4, m2);
+    ld_half(128, e);
+    st_half(LY::T3, e);      // M rows
+    ld_half(192, e);
+    st_half(LY::T4, e);      // M^T rows
   }
   tc::fence_proxy_async_smem();
   tc::tc_fence_before();
   __syncthreads();
-  PTRACE(5);
-  // ---- round 3: F = E M^2 -> cols 128..191 (B rows: (M^2)^T) ----
+  // ---- round 2: Q = D^T M -> cols 128..191, (M^2)^T = M^T M^T -> cols 192..255 ----
+  if (ok && tid == 0) {
+    tc::tc_fence_after();
+    tf32_product(128, LY::T2, LY::T4);
+    tf32_product(192, LY::T4, LY::T3);
+    tc::tc_commit(&ms.mma_bar);
+  }
+  if (ok) mma_wait();
+  PTRACE(6);
+  if (ok) {
+    // E = D^T - Q (half-row r), kept in registers and as the A rows of round 3
+    float dt[32];
+#pragma unroll
+    for (int c8 = 0; c8 < 4; ++c8) ld_f32x8(sm + LY::T2, r, 4 * hc + c8, dt + 8 * c8);
+    ld_half(128, e);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) e[i] = dt[i] - e[i];
+    st_half(LY::QT, e);
+    float m2[32];
+    ld_half(192, m2);
+    st_half(LY::T4, m2);     // (M^2)^T rows
+  }
+  tc::fence_proxy_async_smem();
+  tc::tc_fence_before();
+  __syncthreads();
+  // ---- round 3: F = E M^2 -> cols 128..191 ----
   if (ok && tid == 0) {
     tc::tc_fence_after();
     tf32_product(128, LY::QT, LY::T4);
     tc::tc_commit(&ms.mma_bar);
   }
-  if (ok) { ++mma_uses; mma_wait(); PTRACE(30 + mma_uses); }
+  if (ok) mma_wait();
+  PTRACE(7);
   if (ok) {
-    // (I + A)^-1 transposed: row r = E_r + F_r, bf16 -> the Ai^T tile (one 64-column atom at QT)
-    float f[64];
-    ld_row64(128, f);
-    if (rowt) {
+    // (I + A)^-1 transposed, half-row r = E + F -> bf16 Ai^T tile (one 64-column atom at QT)
+    float f[32];
+    ld_half(128, f);
 #pragma unroll
-      for (int ch = 0; ch < 8; ++ch) {
-        uint32_t w[4];
+    for (int c8 = 0; c8 < 4; ++c8) {
+      uint32_t w[4];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) w[q] = pack_bf16(e[8 * ch + 2 * q] + f[8 * ch + 2 * q], e[8 * ch + 2 * q + 1] + f[8 * ch + 2 * q + 1]);
-        *reinterpret_cast<uint4*>(sm + LY::QT + swz(r, ch)) = make_uint4(w[0], w[1], w[2], w[3]);
-      }
+      for (int q = 0; q < 4; ++q)
+        w[q] = pack_bf16(e[8 * c8 + 2 * q] + f[8 * c8 + 2 * q], e[8 * c8 + 2 * q + 1] + f[8 * c8 + 2 * q + 1]);
+      *reinterpret_cast<uint4*>(sm + LY::QT + swz(r, 4 * hc + c8)) = make_uint4(w[0], w[1], w[2], w[3]);
     }
     // k rows -> bf16(bf16(k beta) e^g) (wy_fast.py:77-79), v rows -> bf16(v beta) (:67), in place
     {
@@ -504,7 +490,6 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_tc_kernel(const __grid_consta
   tc::fence_proxy_async_smem();
   tc::tc_fence_before();
   __syncthreads();
-  PTRACE(6);
   // ---- w = Ai (beta e^g k) -> cols 0..127 (M64 N128); u^T = (beta v)^T Ai^T -> cols
   // 128 + 64 s (M128 N64 per 128-wide V slice s).  Ai^T rows are Ai's MN-major image. ----
   if (ok && tid == 0) {
@@ -523,60 +508,57 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_tc_kernel(const __grid_consta
     }
     tc::tc_commit(&ms.mma_bar);
   }
-  if (ok) { ++mma_uses; mma_wait(); PTRACE(30 + mma_uses); }
+  if (ok) mma_wait();
+  PTRACE(8);
   if (ok) {
-    // w row r -> W blob (bf16, [2 atoms][64 rows][128 B] swizzled); the TMEM loads are
-    // warp-collective, only the row lanes store
-    unsigned char* wb = reinterpret_cast<unsigned char*>(p.wb) + ((size_t)c * H + h) * W_BYTES;
+    // w row r, columns 64 hc .. 64 hc + 63 -> W blob atom hc (bf16, 128-byte swizzle)
+    unsigned char* wb = reinterpret_cast<unsigned char*>(p.wb) + ((size_t)c * H + h) * W_BYTES + hc * 8192;
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      uint32_t u[64];
-      tc::tmem_ld32(tl + 64 * half, u);
-      tc::tmem_ld32(tl + 64 * half + 32, u + 32);
+    for (int q = 0; q < 2; ++q) {
+      uint32_t u[32];
+      tc::tmem_ld16x32bx2_x32<64>(tq + 32 * q, u);
       tc::tmem_wait_ld();
-      if (rowt) {
 #pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
-          uint4 o;
-          o.x = pack_bf16(__uint_as_float(u[8 * ch]), __uint_as_float(u[8 * ch + 1]));
-          o.y = pack_bf16(__uint_as_float(u[8 * ch + 2]), __uint_as_float(u[8 * ch + 3]));
-          o.z = pack_bf16(__uint_as_float(u[8 * ch + 4]), __uint_as_float(u[8 * ch + 5]));
-          o.w = pack_bf16(__uint_as_float(u[8 * ch + 6]), __uint_as_float(u[8 * ch + 7]));
-          *reinterpret_cast<uint4*>(wb + half * 8192 + swz(r, ch)) = o;
-        }
+      for (int c8 = 0; c8 < 4; ++c8) {
+        uint4 o;
+        o.x = pack_bf16(__uint_as_float(u[8 * c8]), __uint_as_float(u[8 * c8 + 1]));
+        o.y = pack_bf16(__uint_as_float(u[8 * c8 + 2]), __uint_as_float(u[8 * c8 + 3]));
+        o.z = pack_bf16(__uint_as_float(u[8 * c8 + 4]), __uint_as_float(u[8 * c8 + 5]));
+        o.w = pack_bf16(__uint_as_float(u[8 * c8 + 6]), __uint_as_float(u[8 * c8 + 7]));
+        *reinterpret_cast<uint4*>(wb + swz(r, 4 * q + c8)) = o;
       }
     }
     // u^T row v = tid (M = 128: all lanes) -> U^T blob ([V rows][64 tokens] bf16 swizzled)
+    const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
     unsigned char* ub = reinterpret_cast<unsigned char*>(p.ub) + ((size_t)c * H + h) * (size_t)(V * 128);
 #pragma unroll
     for (int vs = 0; vs < V / 128; ++vs) {
-      uint32_t u[64];
-      tc::tmem_ld32(tl + 128 + 64 * vs, u);
-      tc::tmem_ld32(tl + 128 + 64 * vs + 32, u + 32);
-      tc::tmem_wait_ld();
 #pragma unroll
-      for (int ch = 0; ch < 8; ++ch) {
-        uint4 o;
-        o.x = pack_bf16(__uint_as_float(u[8 * ch]), __uint_as_float(u[8 * ch + 1]));
-        o.y = pack_bf16(__uint_as_float(u[8 * ch + 2]), __uint_as_float(u[8 * ch + 3]));
-        o.z = pack_bf16(__uint_as_float(u[8 * ch + 4]), __uint_as_float(u[8 * ch + 5]));
-        o.w = pack_bf16(__uint_as_float(u[8 * ch + 6]), __uint_as_float(u[8 * ch + 7]));
-        *reinterpret_cast<uint4*>(ub + vs * 16384 + swz(tid, ch)) = o;
+      for (int q = 0; q < 2; ++q) {
+        uint32_t u[32];
+        tc::tmem_ld32(tl + 128 + 64 * vs + 32 * q, u);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int c8 = 0; c8 < 4; ++c8) {
+          uint4 o;
+          o.x = pack_bf16(__uint_as_float(u[8 * c8]), __uint_as_float(u[8 * c8 + 1]));
+          o.y = pack_bf16(__uint_as_float(u[8 * c8 + 2]), __uint_as_float(u[8 * c8 + 3]));
+          o.z = pack_bf16(__uint_as_float(u[8 * c8 + 4]), __uint_as_float(u[8 * c8 + 5]));
+          o.w = pack_bf16(__uint_as_float(u[8 * c8 + 6]), __uint_as_float(u[8 * c8 + 7]));
+          *reinterpret_cast<uint4*>(ub + vs * 16384 + swz(tid, 4 * q + c8)) = o;
+        }
       }
     }
   }
   tc::tc_fence_before();
   __syncthreads();
-  PTRACE(7);
-  bool keep = false;
+  PTRACE(9);
   if (!ok && mma_uses > 0 && tid == 0) {
     // a wait gave up with MMAs issued: one more (bounded) wait for their completion
     // before TMEM may be freed
-    keep = !wait_(&ms.mma_bar, (mma_uses - 1) & 1);
-    ms.abort = keep;
+    ms.abort = !wait_(&ms.mma_bar, (mma_uses - 1) & 1);
   }
   __syncthreads();
-  PTRACE(8);
   if (warp == 0 && !ms.abort) {
     tc::tc_fence_after();
     tc::tmem_dealloc(tmem, LY::TMEM_COLS);
