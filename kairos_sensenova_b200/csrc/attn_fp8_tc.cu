@@ -1,25 +1,27 @@
 // attn_fp8_tc.cu -- softmax attention forward on 5th-generation tensor cores
 // (tcgen05 + TMEM + TMA), sm_100a: e4m3 Q K^T, bf16 P V, fp32 accumulation.
 //
-// One CTA per (two 128-query tiles, batch*head); keys in tiles of BN = 64.
+// One CTA per (two 128-query tiles, batch*head); keys in tiles of BN = 128.
 //   warps 16, 18: TMA producers (Q once and K per key tile; V^T per key tile),
 //                 each into its own ring
 //   warps 17, 19: MMA issuers (one elected thread each, one per query tile t);
 //                 warp 17 also owns TMEM
-//                 S_t = Q_t K_j^T  -> TMEM S[t]   (kind::f8f6f4, e4m3, M128 N64 K32)
+//                 S_t = Q_t K_j^T  -> TMEM S[t]   (kind::f8f6f4, e4m3, M128 N128 K32)
 //                 O_t += P_t V_j   -> TMEM O[t]   (kind::f16, bf16; A = P_t read
 //                                                  from TMEM, B = V^T from smem)
-//   warps 0..15 : softmax, four warpgroups: (query tile t, key half) -- each
-//                 thread owns 32 scores of one row (TMEM lane): S from TMEM ->
-//                 (running max only when a norm bound says it may have grown; the
-//                 two halves of a row then exchange their maxima) -> P = 2^(s - m +
-//                 SHIFT) in bf16 into TMEM P[t] -> final O / l -> bf16.  Four
-//                 softmax warps per scheduler hide the latency of the exponential
-//                 chains.
-// With S, P and O in separate TMEM columns the MMA issuer computes S(j+1) while
-// the softmax works on S(j), and PV(j) runs while it works on S(j+1); the
-// probabilities never touch shared memory, whose bandwidth the tensor cores'
-// operand reads already need.
+//   warps 0..15 : softmax, four warpgroups (query tile t, key half): each thread
+//                 owns the 64 scores of one row in its key half (TMEM lane): S
+//                 from TMEM -> (running max only when a norm bound says it may
+//                 have grown; the two halves of a row then exchange their
+//                 maxima) -> P = 2^(s - m + SHIFT) in bf16, written back into the
+//                 first 32 of its 64 S columns -> final O / l -> bf16.
+// P aliases S: the probabilities of key tile j are packed (two bf16 per column)
+// into the first half of each key half's S columns, so S, P and O of both query
+// tiles fit the 512 TMEM columns with 128-key tiles.  Per query tile the chain is
+// QK(j) -> softmax(j) -> PV(j) -> QK(j+1), with QK(j+1) issued directly behind PV(j)
+// (tcgen05.mma operations of one thread execute in order, so PV(j) has read P before
+// QK(j+1) overwrites it).  The two query tiles take turns with their exponentials,
+// so one tile's softmax overlaps the other's matrix products on the tensor pipe.
 //
 // Every mbarrier wait is bounded; a wait that gives up records an error code in
 // the workspace and the CTA skips the rest of its work.  Before it exits, the
@@ -34,8 +36,8 @@
 namespace kb {
 namespace attn {
 
-constexpr int TC_BM = 128, TC_BN = 64, TC_D = 128;
-constexpr int TC_QT = 2;          // query tiles per CTA (two softmax warpgroups)
+constexpr int TC_BM = 128, TC_BN = 128, TC_D = 128;
+constexpr int TC_QT = 2;          // query tiles per CTA (ping-pong)
 constexpr float TC_SHIFT = 6.f;   // P = 2^(s - m + SHIFT)
 // Lazy-rescale threshold (log2 units): O and l are rescaled only when the
 // running max grows by more than TAU, so P <= 2^(SHIFT+TAU) = 2^46 and a row sum
@@ -44,35 +46,34 @@ constexpr float TC_SHIFT = 6.f;   // P = 2^(s - m + SHIFT)
 // give bounds ~15 log2 units above the first tile's max), so the exact row max is
 // rarely needed.
 constexpr float TC_TAU = 40.f;
-// Which score pairs of every 8 take the FMA-pipe polynomial instead of MUFU ex2.
+// Which score pairs of every 8 take the FMA-pipe polynomial instead of MUFU ex2
+// (one of four: measured best with the query tiles taking turns).
 #ifndef KB_ATTN_POLY_MASK
-#define KB_ATTN_POLY_MASK 0x0
+#define KB_ATTN_POLY_MASK 0x1
 #endif
 constexpr int TC_POLY_MASK = KB_ATTN_POLY_MASK;
-// TMEM columns: S_t [64 t, 64 t + 64), P_t in two buffers [128 + 64 t + 32 b, +32) (bf16
-// pairs; tile j uses buffer j & 1), O_t [256 + 128 t, +128).
-constexpr uint32_t TM_S = 0, TM_P = 128, TM_O = 256;
+// TMEM columns: S_t (and P_t aliased into it) [128 t, 128 t + 128), O_t [256 + 128 t, +128).
+constexpr uint32_t TM_S = 0, TM_O = 256;
 
 struct TcSmem {
-  // K and V^T have separate rings: a K tile is free once both QK products that
-  // read it are done, a V tile only after both PV products.
-  static constexpr int KS = 6, VS = 6;
-  uint8_t q[TC_QT][TC_BM * TC_D];               // e4m3 q                     SW128 K-major, 128 rows
-  uint8_t k[KS][TC_BN * TC_D];                  // e4m3 k tiles               SW128 K-major, 64 rows
-  __nv_bfloat16 v[VS][TC_D * TC_BN];            // bf16 v^T tiles             SW128 K-major (64 keys = 128 B)
+  static constexpr int KS = 4, VS = 3;
+  uint8_t q[TC_QT][TC_BM * TC_D];               // e4m3 q               SW128 K-major, 128 rows
+  uint8_t k[KS][TC_BN * TC_D];                  // e4m3 k tiles         SW128 K-major, 128 rows
+  __nv_bfloat16 v[VS][2][TC_D * 64];            // bf16 v^T tiles: 2 atoms of 64 keys x 128 rows
   uint64_t q_full;
   uint64_t k_full[KS], k_empty[KS], v_full[VS], v_empty[VS];
-  // p_full[t][b]: P of tile j is in TMEM buffer b = j & 1 (phase j >> 1).  One barrier
-  // per buffer: the softmax may publish tile j+1 before the MMA issuer consumed tile
-  // j, but never tile j+2 (that needs S(j+2), issued after PV(j)).
-  uint64_t s_full[TC_QT], s_free[TC_QT], p_full[TC_QT][2], pv_done[TC_QT];
-  uint64_t o_done[TC_QT];                       // one phase: every PV of the tile completed
+  uint64_t s_full[TC_QT], p_full[TC_QT], o_done[TC_QT];
+  // turn[t]: the other query tile finished its exponentials of a key tile.  The two
+  // softmax groups take turns (tile 0 key tile j, tile 1 key tile j, tile 0 key tile
+  // j + 1, ...), so one group's exponentials run while the other tile's products use
+  // the tensor pipe, instead of both contending for the MUFU unit at once.
+  uint64_t turn[TC_QT];
   uint64_t xbar[TC_QT][4];                      // per (tile, lane quarter): the two key halves of a row exchange a value
   float xch[TC_QT][2][2][TC_BM];                // [tile][use parity][half][row]
-  uint64_t drain[TC_QT];                        // abort-safe exit: every MMA of issuer t completed
+  uint64_t drain[TC_QT];
   uint32_t tmem_base;
   int abort_flag;
-  int keep_tmem;                                // a drain wait gave up: TMEM may still be written, do not free it
+  int keep_tmem;
 };
 
 struct TcMaps {
@@ -80,9 +81,11 @@ struct TcMaps {
 };
 
 #ifdef KB_ATTN_TRACE
-#define TRACE(slot, j) do { if (p.trace && blockIdx.x == 0 && blockIdx.y == 0) p.trace[(j) * 16 + (slot)] = clock64(); } while (0)
+__device__ long long* g_attn_trace;
+#define ATRACE(j, slot) do { if (g_attn_trace && blockIdx.x == 3 && blockIdx.y == 5 && (j) < 128) \
+  g_attn_trace[(j) * 16 + (slot)] = clock64(); } while (0)
 #else
-#define TRACE(slot, j) do { } while (0)
+#define ATRACE(j, slot) do { } while (0)
 #endif
 
 template <class S>
@@ -133,7 +136,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_fp8_tc_kernel(const __grid
   using SM = TcSmem;
   constexpr int KS = SM::KS, VS = SM::VS;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  SM& sm = *reinterpret_cast<SM*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1024-align by pointer arithmetic on the shared array (keeps shared addressing)
+  SM& sm = *reinterpret_cast<SM*>(smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
   const int q0 = blockIdx.x * (TC_QT * TC_BM);
@@ -151,13 +155,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_fp8_tc_kernel(const __grid
     }
     for (int i = 0; i < TC_QT; ++i) {
       tc::mbar_init(&sm.s_full[i], 1);
-      tc::mbar_init(&sm.s_free[i], 256);
-      tc::mbar_init(&sm.p_full[i][0], 256);
-      tc::mbar_init(&sm.p_full[i][1], 256);
-      tc::mbar_init(&sm.pv_done[i], 1);
+      tc::mbar_init(&sm.p_full[i], 256);
       tc::mbar_init(&sm.o_done[i], 1);
-      for (int w = 0; w < 4; ++w) tc::mbar_init(&sm.xbar[i][w], 64);
       tc::mbar_init(&sm.drain[i], 1);
+      tc::mbar_init(&sm.turn[i], 256);
+      for (int w = 0; w < 4; ++w) tc::mbar_init(&sm.xbar[i][w], 64);
     }
     sm.abort_flag = 0;
     sm.keep_tmem = 0;
@@ -171,6 +173,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_fp8_tc_kernel(const __grid
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
+  auto aborted = [&]() { return *((volatile int*)&sm.abort_flag) != 0; };
 
   if (warp == 16) {
     // ------------------------------------------------------------ TMA producer of Q and K
@@ -184,13 +187,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_fp8_tc_kernel(const __grid
       for (int j = 0; j < ntiles; ++j) {
         const int st = j % KS, use = j / KS;
         if (j >= KS && !tc::mbar_wait(&sm.k_empty[st], (use - 1) & 1)) { fail(sm, err, 11); break; }
-        if (sm.abort_flag) break;
+        if (aborted()) break;
         tc::mbar_expect_tx(&sm.k_full[st], TC_BN * TC_D);
         tc::tma_load_2d(sm.k[st], &maps.k, &sm.k_full[st], 0, bh * p.S_pad + j * TC_BN);
         ++issued;
       }
-      // before the CTA may exit, every load it issued must have landed (on the normal
-      // path they all have; after an abort the last load of each slot may be in flight)
+      // before the CTA may exit, every load it issued must have landed
       bool drained = tc::mbar_wait(&sm.q_full, 0);
       for (int j = issued > KS ? issued - KS : 0; j < issued; ++j)
         drained &= tc::mbar_wait(&sm.k_full[j % KS], (j / KS) & 1);
@@ -204,9 +206,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_fp8_tc_kernel(const __grid
       for (int j = 0; j < ntiles; ++j) {
         const int st = j % VS, use = j / VS;
         if (j >= VS && !tc::mbar_wait(&sm.v_empty[st], (use - 1) & 1)) { fail(sm, err, 16); break; }
-        if (sm.abort_flag) break;
+        if (aborted()) break;
         tc::mbar_expect_tx(&sm.v_full[st], 2 * TC_BN * TC_D);
-        tc::tma_load_2d(sm.v[st], &maps.vt, &sm.v_full[st], j * TC_BN, bh * TC_D);
+        tc::tma_load_2d(sm.v[st][0], &maps.vt, &sm.v_full[st], j * TC_BN, bh * TC_D);
+        tc::tma_load_2d(sm.v[st][1], &maps.vt, &sm.v_full[st], j * TC_BN + 64, bh * TC_D);
         ++issued;
       }
       bool drained = true;
@@ -216,76 +219,69 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_fp8_tc_kernel(const __grid
     }
   } else if (warp == 17 || warp == 19) {
     // ------------------------------------------------------------ MMA issuers
-    // One thread per query tile: QK(j) as soon as K_j landed and the softmax has
-    // read S(j-1), then PV(j-1) once P(j-1) is in TMEM.  Both feed the same
-    // tensor pipe.
+    // One thread per query tile: QK(j) once K_j landed, then PV(j) once the softmax
+    // published P(j).  s_full(j) tracks every earlier MMA of the thread, so when the
+    // softmax sees S(j), PV(j-1) has completed too (O may be rescaled).
     if (lane == 0) {
       const int qt = warp == 17 ? 0 : 1;
       constexpr uint32_t IDESC_QK = tc::idesc_e4m3_f32(TC_BM, TC_BN);
       constexpr uint32_t IDESC_PV = tc::idesc_bf16_f32(TC_BM, TC_D);
-      const uint32_t tS = tmem + TM_S + qt * TC_BN, tP = tmem + TM_P + qt * TC_BN,
-                     tO = tmem + TM_O + qt * TC_D;
+      const uint32_t tS = tmem + TM_S + qt * 128, tO = tmem + TM_O + qt * TC_D;
       const uint64_t dq = tc::sdesc_sw128_kmajor(sm.q[qt]);
       bool ok = tc::mbar_wait(&sm.q_full, 0);
       if (!ok) fail(sm, err, 12);
-      for (int j = 0; ok && j <= ntiles; ++j) {
-        if (j < ntiles) {
-          const int st = j % KS;
-          if (!tc::mbar_wait(&sm.k_full[st], (j / KS) & 1)) { fail(sm, err, 14); ok = false; break; }
-          if (j >= 1 && !tc::mbar_wait(&sm.s_free[qt], (j - 1) & 1)) { fail(sm, err, 15); ok = false; break; }
-          if (sm.abort_flag) { ok = false; break; }
-          tc::tc_fence_after();
-          const uint64_t dk = tc::sdesc_sw128_kmajor(sm.k[st]);
+      for (int j = 0; ok && j < ntiles; ++j) {
+        const int st = j % KS, sv = j % VS;
+        if (!tc::mbar_wait(&sm.k_full[st], (j / KS) & 1)) { fail(sm, err, 14); ok = false; break; }
+        if (aborted()) { ok = false; break; }
+        // QK(j) writes the S columns that PV(j-1) reads P from: tcgen05.mma operations
+        // of one thread execute in issue order, so it is issued right behind PV(j-1)
+        tc::tc_fence_after();
+        const uint64_t dk = tc::sdesc_sw128_kmajor(sm.k[st]);
 #pragma unroll
-          for (int ks = 0; ks < TC_D / 32; ++ks)
-            tc::mma_f8f6f4(tS, dq + 2 * ks, dk + 2 * ks, IDESC_QK, ks > 0 ? 1u : 0u);
-          tc::tc_commit(&sm.s_full[qt]);
-          tc::tc_commit(&sm.k_empty[st]);
-          TRACE(qt, j);
-        }
-        if (j >= 1) {
-          const int jj = j - 1, sv = jj % VS;
-          if (!tc::mbar_wait(&sm.v_full[sv], (jj / VS) & 1)) { fail(sm, err, 17); ok = false; break; }
-          if (!tc::mbar_wait(&sm.p_full[qt][jj & 1], (jj >> 1) & 1)) { fail(sm, err, 13); ok = false; break; }
-          tc::tc_fence_after();
-          const uint64_t dv = tc::sdesc_sw128_kmajor(sm.v[sv]);
-          // K = 16 keys per instruction: 8 TMEM columns of packed bf16 P, 32 B of a V^T row
+        for (int ks = 0; ks < TC_D / 32; ++ks)
+          tc::mma_f8f6f4(tS, dq + 2 * ks, dk + 2 * ks, IDESC_QK, ks > 0 ? 1u : 0u);
+        tc::tc_commit(&sm.s_full[qt]);
+        tc::tc_commit(&sm.k_empty[st]);
+        ATRACE(j, 0 + qt * 8);
+        if (!tc::mbar_wait(&sm.v_full[sv], (j / VS) & 1)) { fail(sm, err, 17); ok = false; break; }
+        if (!tc::mbar_wait(&sm.p_full[qt], j & 1)) { fail(sm, err, 13); ok = false; break; }
+        if (aborted()) { ok = false; break; }
+        tc::tc_fence_after();
+        // K = 16 keys per instruction: 8 TMEM columns of packed bf16 P (key half kh at
+        // columns 64 kh .. 64 kh + 31), 32 B of a V^T row in atom kh
 #pragma unroll
-          for (int ks = 0; ks < TC_BN / 16; ++ks)
-            tc::mma_bf16_ts(tO, tP + (jj & 1) * (TC_BN / 2) + ks * 8, dv + 2 * ks, IDESC_PV,
-                            (jj > 0 || ks > 0) ? 1u : 0u);
-          tc::tc_commit(&sm.pv_done[qt]);
-          tc::tc_commit(&sm.v_empty[sv]);
-          TRACE(2 + qt, jj);
+        for (int ks = 0; ks < TC_BN / 16; ++ks) {
+          const int kh = ks >> 2;
+          const uint64_t dv = tc::sdesc_sw128_kmajor(sm.v[sv][kh]);
+          tc::mma_bf16_ts(tO, tS + kh * 64 + (ks & 3) * 8, dv + 2 * (ks & 3), IDESC_PV, (j > 0 || ks > 0) ? 1u : 0u);
         }
+        tc::tc_commit(&sm.v_empty[sv]);
+        ATRACE(j, 1 + qt * 8);
       }
       if (ok) tc::tc_commit(&sm.o_done[qt]);
-      // every MMA this thread issued must complete before TMEM is freed (after an
-      // abort some may still be running)
+      // every MMA this thread issued must complete before TMEM is freed
       tc::tc_commit(&sm.drain[qt]);
       if (!tc::mbar_wait(&sm.drain[qt], 0)) { fail(sm, err, 20); sm.keep_tmem = 1; }
     }
   } else {
     // ------------------------------------------------------------ softmax (warps 0..15)
     const int qt = (warp >> 2) & 1;                  // query tile
-    const int half = warp >> 3;                      // key half: columns [32 half, 32 half + 32) of S
+    const int half = warp >> 3;                      // key half: columns [64 half, 64 half + 64) of S
     const int r = (warp & 3) * 32 + lane;            // row in the tile == TMEM lane
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-    const uint32_t tS = tmem + TM_S + qt * TC_BN + half * 32 + lane_off,
-                   tP = tmem + TM_P + qt * TC_BN + half * 16 + lane_off,
+    const uint32_t tS = tmem + TM_S + qt * 128 + half * 64 + lane_off,
                    tO = tmem + TM_O + qt * TC_D + lane_off;
     const float sq = scale_of(p.amax[(0 * p.B + b) * p.H + h]);
     const float sk = scale_of(p.amax[(1 * p.B + b) * p.H + h]);
     const float sl2 = sq * sk * p.softmax_scale * 1.4426950408889634f;   // raw score -> log2 units
     const float qb = 1.0625f * p.qn[(size_t)bh * p.S_pad + q0 + qt * TC_BM + r] + 0.012f;
-    const float* knp = p.kn + (size_t)bh * (p.S_pad / TC_BN);
+    const float* knp = p.kn + (size_t)bh * (p.S_pad / 64);
+    const int nk64 = p.S_pad / 64;
     float m_ref = -INFINITY, l = 0.f;
-    float kn_next = knp[0];   // key-norm bound of the coming tile, loaded one tile ahead
-    int xuse = 0;             // exchanges done so far (both halves of a row make the same ones)
+    float kn_next = fmaxf(knp[0], knp[min(1, nk64 - 1)]);   // key-norm bound of the coming 128-key tile
+    int xuse = 0;
     bool ok = true;
-    // the other half's value of this row: both warps of the pair (same rows, the
-    // two key halves) write, arrive, and read (bounded wait); the pair makes the
-    // same sequence of exchanges because it takes the same branches
     uint64_t* xb = &sm.xbar[qt][warp & 3];
     auto exchange = [&](float v) -> float {
       float* slot = sm.xch[qt][xuse & 1][0];
@@ -298,23 +294,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_fp8_tc_kernel(const __grid
     };
     for (int j = 0; j < ntiles; ++j) {
       const float kn_j = kn_next;
-      kn_next = knp[min(j + 1, ntiles - 1)];
-      if (r == 0 && half == 0) TRACE(4 + qt * 5, j);
+      const int jn = min(j + 1, ntiles - 1);
+      kn_next = fmaxf(knp[min(2 * jn, nk64 - 1)], knp[min(2 * jn + 1, nk64 - 1)]);
+      if (r == 0 && half == 0) ATRACE(j, 2 + qt * 8);
       if (!tc::mbar_wait(&sm.s_full[qt], j & 1)) { fail(sm, err, 21); ok = false; }
-      if (r == 0 && half == 0) TRACE(5 + qt * 5, j);
-      if (__any_sync(0xffffffffu, !ok || sm.abort_flag)) { ok = false; break; }
+      // my turn: tile 0 after tile 1 finished key tile j - 1, tile 1 after tile 0 finished j
+      if (qt == 0 ? j >= 1 : true)
+        if (!tc::mbar_wait(&sm.turn[qt], (qt == 0 ? j - 1 : j) & 1)) { fail(sm, err, 27); ok = false; }
+      if (r == 0 && half == 0) ATRACE(j, 3 + qt * 8);
+      if (__any_sync(0xffffffffu, !ok || aborted())) { ok = false; break; }
       tc::tc_fence_after();
-      uint32_t s[32];
-      tc::tmem_ld32(tS, s);
-      tc::tmem_wait_ld();
-      tc::tc_fence_before();
-      tc::mbar_arrive(&sm.s_free[qt]);
-      const int kvalid = p.S - j * TC_BN - half * 32;
-      if (kvalid < 32) {
-#pragma unroll
-        for (int c = 0; c < 32; ++c)
-          if (c >= kvalid) s[c] = __float_as_uint(-INFINITY);
-      }
+      const int kvalid = p.S - j * TC_BN - half * 64;
       // Every score of this tile is at most |sl2| |q8_row| max|k8| (Cauchy-Schwarz on the
       // e4m3 vectors the MMA multiplies; the factors cover e4m3 rounding of the stored
       // unrounded norms and the fp32 accumulation).  While that bound stays within TAU
@@ -322,17 +312,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_fp8_tc_kernel(const __grid
       // halves of a row evaluate the same bound, so they take the same branch.
       bool need_max = j == 0;
       if (!need_max) {
-        const float kb = 1.0625f * kn_j + 0.012f;
-        need_max = __any_sync(0xffffffffu, fabsf(sl2) * qb * kb * 1.001f > m_ref + TC_TAU);
+        const float kbd = 1.0625f * kn_j + 0.012f;
+        need_max = __any_sync(0xffffffffu, fabsf(sl2) * qb * kbd * 1.001f > m_ref + TC_TAU);
       }
       float alpha = 1.f;
       if (need_max) {
-        float mx[8];
+        float mpart = -INFINITY;
+#pragma unroll 1
+        for (int part = 0; part < 2; ++part) {
+          uint32_t s[32];
+          tc::tmem_ld32(tS + 32 * part, s);
+          tc::tmem_wait_ld();
 #pragma unroll
-        for (int z = 0; z < 8; ++z)
-          mx[z] = fmax3(__uint_as_float(s[z]), __uint_as_float(s[z + 8]),
-                        fmaxf(__uint_as_float(s[z + 16]), __uint_as_float(s[z + 24])));
-        const float mpart = fmaxf(fmax3(mx[0], mx[1], mx[2]), fmax3(fmax3(mx[3], mx[4], mx[5]), mx[6], mx[7]));
+          for (int c = 0; c < 32; ++c)
+            if (32 * part + c < kvalid) mpart = fmaxf(mpart, __uint_as_float(s[c]));
+        }
         const float mraw = fmaxf(mpart, exchange(mpart));
         if (__any_sync(0xffffffffu, !ok)) break;
         const float m_new = fmaxf(m_ref, mraw * sl2);
@@ -342,55 +336,62 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_fp8_tc_kernel(const __grid
           l *= alpha;
         }
       }
-      // exponentials: per 8 scores, 4 on the MUFU unit and 4 as a polynomial on
-      // the FMA pipe; scaling and row sums as f32x2; P packed as bf16 pairs
+      // exponentials: P packed as bf16 pairs; scaling and row sums as f32x2.  The two
+      // 32-score parts are read before P overwrites the first of them.
       const float bias = TC_SHIFT - m_ref;
       const float2 sl2v = make_float2(sl2, sl2), biasv = make_float2(bias, bias);
       float2 ls0 = make_float2(0.f, 0.f), ls1 = make_float2(0.f, 0.f);
-      uint32_t pk[16];
 #pragma unroll
-      for (int c = 0; c < 32; c += 8) {
-        float2 x[4];
+      for (int part = 0; part < 2; ++part) {
+        uint32_t pk[16];
+        uint32_t s[32];
+        tc::tmem_ld32(tS + 32 * part, s);
+        tc::tmem_wait_ld();
+        const int kv = kvalid - 32 * part;
+        if (kv < 32) {
 #pragma unroll
-        for (int z = 0; z < 4; ++z)
-          x[z] = ffma2(make_float2(__uint_as_float(s[c + 2 * z]), __uint_as_float(s[c + 2 * z + 1])), sl2v, biasv);
-        float2 e[4];
+          for (int c = 0; c < 32; ++c)
+            if (c >= kv) s[c] = __float_as_uint(-INFINITY);
+        }
 #pragma unroll
-        for (int z = 0; z < 4; ++z)
-          e[z] = ((TC_POLY_MASK >> z) & 1) ? exp2_poly2(x[z]) : make_float2(ex2(x[z].x), ex2(x[z].y));
-        ls0 = fadd2(ls0, fadd2(e[0], e[1]));
-        ls1 = fadd2(ls1, fadd2(e[2], e[3]));
+        for (int c = 0; c < 32; c += 8) {
+          float2 x[4];
 #pragma unroll
-        for (int z = 0; z < 4; ++z) pk[c / 2 + z] = pack_bf16(e[z].x, e[z].y);
+          for (int z = 0; z < 4; ++z)
+            x[z] = ffma2(make_float2(__uint_as_float(s[c + 2 * z]), __uint_as_float(s[c + 2 * z + 1])), sl2v, biasv);
+          float2 e[4];
+#pragma unroll
+          for (int z = 0; z < 4; ++z)
+            e[z] = ((TC_POLY_MASK >> z) & 1) ? exp2_poly2(x[z]) : make_float2(ex2(x[z].x), ex2(x[z].y));
+          ls0 = fadd2(ls0, fadd2(e[0], e[1]));
+          ls1 = fadd2(ls1, fadd2(e[2], e[3]));
+#pragma unroll
+          for (int z = 0; z < 4; ++z) pk[c / 2 + z] = pack_bf16(e[z].x, e[z].y);
+        }
+        // P of these 32 keys -> 16 columns at the start of the part-0 S columns (part 1's
+        // S columns, 32..63, are read before anything is written there)
+        tc::tmem_st16(tS + 16 * part, pk);
       }
-      if (r == 0 && half == 0) TRACE(6 + qt * 5, j);
+      tc::mbar_arrive(&sm.turn[qt ^ 1]);   // the exponentials of this key tile are done
       const float2 lsum = fadd2(ls0, ls1);
       l += lsum.x + lsum.y;
-      // P buffer j & 1 was last read by PV(j-2), which s_full(j) already covers.  A
-      // rescale of O needs PV(j-1) complete as well (pv_done has completed j-1 or j
-      // phases here, so the parity test is exact).
-      if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.f)) {
-        if (!tc::mbar_wait(&sm.pv_done[qt], (j - 1) & 1)) { fail(sm, err, 22); ok = false; }
-        if (__any_sync(0xffffffffu, !ok)) { ok = false; break; }
-        tc::tc_fence_after();
-        if (half == 0) {   // O *= alpha before PV(j) adds into it
+      // O *= alpha before PV(j) adds into it (s_full(j) covers PV(j-1))
+      if (__any_sync(0xffffffffu, alpha != 1.f) && half == 0 && j >= 1) {
 #pragma unroll 1
-          for (int c = 0; c < TC_D / 32; ++c) {
-            uint32_t o[32];
-            tc::tmem_ld32(tO + c * 32, o);
-            tc::tmem_wait_ld();
+        for (int c = 0; c < TC_D / 32; ++c) {
+          uint32_t o[32];
+          tc::tmem_ld32(tO + c * 32, o);
+          tc::tmem_wait_ld();
 #pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-            tc::tmem_st32(tO + c * 32, o);
-          }
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tc::tmem_st32(tO + c * 32, o);
         }
       }
-      tc::tmem_st16(tP + (j & 1) * (TC_BN / 2), pk);
+      if (r == 0 && half == 0) ATRACE(j, 4 + qt * 8);
       tc::tmem_wait_st();
-      if (r == 0 && half == 0) TRACE(7 + qt * 5, j);
       tc::tc_fence_before();
-      tc::mbar_arrive(&sm.p_full[qt][j & 1]);
-      if (r == 0 && half == 0) TRACE(8 + qt * 5, j);
+      tc::mbar_arrive(&sm.p_full[qt]);
+      if (r == 0 && half == 0) ATRACE(j, 5 + qt * 8);
     }
     // epilogue: the row sum of both halves; each half writes 64 of the 128 output
     // columns once the last PV has completed
@@ -447,13 +448,19 @@ static int make_map(CUtensorMap* m, const void* base, uint64_t cols, uint64_t ro
   return KB200_OK;
 }
 
+#ifdef KB_ATTN_TRACE
+extern "C" int kb200_attn_set_trace(long long* t) {
+  return cudaMemcpyToSymbol(g_attn_trace, &t, sizeof(t)) == cudaSuccess ? 0 : 4;
+}
+#endif
+
 int launch_attn_tc(const Params& p, int* err, cudaStream_t st) {
   TcMaps maps;
   const uint64_t rows_q = (uint64_t)p.B * p.H * p.S_pad, rows_v = (uint64_t)p.B * p.H * TC_D;
   if (p.S_pad % (TC_QT * TC_BM)) return set_error(KB200_ERR_INVALID, "attn_fp8_tc: S_pad must be a multiple of 256");
   if (int e = make_map(&maps.q, p.q8, TC_D, rows_q, TC_D, 1, TC_BM)) return e;
   if (int e = make_map(&maps.k, p.k8, TC_D, rows_q, TC_D, 1, TC_BN)) return e;
-  if (int e = make_map(&maps.vt, p.vt, p.S_pad, rows_v, (uint64_t)p.S_pad * 2, 2, TC_D)) return e;
+  if (int e = make_map(&maps.vt, p.vt, p.S_pad, rows_v, (uint64_t)p.S_pad * 2, 2, TC_D)) return e;   // boxes: 64 keys x 128 rows
   const size_t smem = sizeof(TcSmem) + 1024;
   cudaFuncSetAttribute(attn_fp8_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   attn_fp8_tc_kernel<<<dim3(p.S_pad / (TC_QT * TC_BM), (unsigned)(p.B * p.H)), TC_THREADS, smem, st>>>(maps, p,
