@@ -21,6 +21,7 @@ from __future__ import annotations
 
 import argparse
 import datetime
+import gc
 import json
 import os
 import statistics
@@ -275,7 +276,9 @@ def time_dit(args, world, rank, sync_all, flush):
     ms = statistics.mean(s0.elapsed_time(s1) for s0, s1 in ev)
     ok = bool(torch.isfinite(out.float()).all())
     n = model.launches_per_step()
-    del model, step
+    del model, step, out
+    gc.collect()
+    sync_all()
     torch.cuda.empty_cache()
     return {'metric': 'DiT denoise-step ms', 'ms_per_step': ms, 'higher_is_better': False,
             'steps': args.dit_steps, 'warmup': warm, 'n_gpus': world, 'finite_output': ok,
@@ -348,14 +351,27 @@ def main():
         sync_all()
         attn_ms = statistics.mean(a0.elapsed_time(a1) for a0, a1 in aev)
         launches = blk.launches_per_step()
-        # the step: one CUDA graph per input buffer (two, ping-ponged by the e2e loop).
-        # With more than one rank the step is issued op by op: in a 2-GPU run with the
-        # hybrid step's graphs (NCCL sends/receives captured inside) still alive at
-        # the end, a rank did not exit after its result was printed; the eager
-        # multi-rank path has always torn down cleanly, and at 2 GPUs both timed the
-        # same (10.2 vs 10.0 ms per step)
+        # per-phase device time (eager steps, CUDA events at the phase boundaries on the
+        # compute stream): where a multi-GPU step spends its time
+        phase_runs = []
+        for _ in range(min(args.steps, 5)):
+            flush.zero_()
+            marks = []
+            blk.forward(x, phases=marks)
+            phase_runs.append(marks)
+        sync_all()
+        phase_ms = {}
+        for marks in phase_runs:
+            for (_, e0), (name, e1) in zip(marks[:-1], marks[1:]):
+                if name.endswith('.start'):
+                    continue
+                phase_ms[name] = phase_ms.get(name, 0.0) + e0.elapsed_time(e1) / len(phase_runs)
+        # the step: one CUDA graph per input buffer (two, ping-ponged by the e2e loop),
+        # at every GPU count.  A graph that captured NCCL sends/receives holds on to the
+        # communicator's resources: the graphs are destroyed (and the device idle) on
+        # every rank before the process group is torn down.
         xd = [x.clone(), x.clone()]
-        eager = args.eager or world > 1
+        eager = args.eager
         if eager:
             steps = [lambda b=b: blk.forward(xd[b]) for b in range(2)]
         else:
@@ -422,8 +438,9 @@ def main():
         sync_all()
         e2e_ms = e0.elapsed_time(e1) / args.steps
         clocks = sampler.stop() if sampler else None
-        del steps
-        torch.cuda.synchronize()
+        del steps, y
+        gc.collect()
+        sync_all()
 
     del blk
     gdn_ms = sdpa_ms = gdn_launches = None
@@ -434,10 +451,14 @@ def main():
         torch.cuda.empty_cache()
     sync_all()
     dit = time_dit(args, world, rank, sync_all, flush) if args.dit_steps > 0 else None
-    t = torch.tensor([step_ms, attn_ms, e2e_ms, dit['ms_per_step'] if dit else 0.0], device='cuda')
+    names = sorted(phase_ms)
+    t = torch.tensor([step_ms, attn_ms, e2e_ms, dit['ms_per_step'] if dit else 0.0] + [phase_ms[n] for n in names],
+                     device='cuda')
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    step_ms, attn_ms, e2e_ms, dit_ms = t.tolist()
+    vals = t.tolist()
+    step_ms, attn_ms, e2e_ms, dit_ms = vals[:4]
+    phase_ms = dict(zip(names, vals[4:]))
     if rank == 0:
         bf16_tf, hbm, kind = _peaks()
         # QK^T (half the FLOPs) runs at the e4m3 rate, 2x bf16; P.V at the bf16 rate
@@ -476,6 +497,8 @@ def main():
                              'tensor_frac': gdn_tf / bf16_tf,
                              'peak_source': f'{kind} HBM copy bandwidth; tensor_frac against {kind} bf16 dense'},
             'clocks': clocks,
+            'phases_ms': {'values': phase_ms, 'how': 'eager steps, CUDA events at phase boundaries on the '
+                                                      'compute stream, mean over steps, max over ranks'},
         }
         if dit:
             dit['ms_per_step'] = dit_ms

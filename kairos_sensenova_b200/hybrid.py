@@ -55,17 +55,18 @@ class HybridBlock:
         self.attn = AttnMixer(self.Aq, self.Ak, self.Av, self.Ao, self.nq, self.nk, heads, head_dim, world,
                               rank, group, attn_eps, grid=grid)
 
-    def gdn_chain(self, x_local):
-        return self.gdn(x_local)
+    def gdn_chain(self, x_local, phases=None):
+        return self.gdn(x_local, phases=phases)
 
-    def attn_chain(self, x_local, events=None):
-        return self.attn(x_local, events)
+    def attn_chain(self, x_local, events=None, phases=None):
+        return self.attn(x_local, events, phases=phases)
 
-    def forward(self, x_local, events=None):
+    def forward(self, x_local, events=None, phases=None):
         """One hybrid step: the GDN chain, then the attention chain on its output.
-        ``events`` (optional start/end pair) brackets the attention kernel."""
-        y = self.gdn_chain(x_local)
-        return self.attn_chain(y, events)
+        ``events`` (optional start/end pair) brackets the attention kernel;
+        ``phases`` (optional list) collects per-phase CUDA event marks."""
+        y = self.gdn_chain(x_local, phases)
+        return self.attn_chain(y, events, phases)
 
     def launches_per_step(self):
         """Kernel launches of this library per forward() (as of the last call)."""

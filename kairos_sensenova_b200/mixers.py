@@ -42,6 +42,19 @@ def _round8(n):
     return (n + 7) // 8 * 8
 
 
+def _marker(phases, prefix):
+    """A function recording a CUDA event named ``prefix.name`` on the current stream
+    into ``phases`` (a no-op when ``phases`` is None)."""
+    if phases is None:
+        return lambda name: None
+
+    def mark(name):
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        phases.append((f'{prefix}.{name}', e))
+    return mark
+
+
 _COMM_STREAMS = {}
 
 
@@ -170,21 +183,32 @@ class GdnMixer(_Ulysses):
         self.WoT = Wo.t().contiguous()
         self.o_norm_w = o_norm_w
 
-    def __call__(self, x_local):
+    def __call__(self, x_local, phases=None):
+        """``phases`` (optional list) receives (name, CUDA event) marks at the phase
+        boundaries on the compute stream: projection + seq->head exchange, prologue,
+        GDN, head->seq exchange, epilogue (gate, norm, o_proj)."""
+        mark = _marker(phases, 'gdn')
         Tl = x_local.shape[0]
         T = Tl * self.P
         Hl, D = self.Hl, self.D
+        mark('start')
         recv = self._project_exchange(x_local, self.W, None)            # [T, C]
+        mark('proj_exchange')
         c = lambda i: recv[:, i * Hl * D:(i + 1) * Hl * D]  # noqa: E731
         ab = 3 * Hl * D
         q, k, v, g, beta = gdn_prologue(c(0), c(1), c(2), recv[:, ab:ab + Hl], recv[:, ab + Hl:ab + 2 * Hl],
                                         self.cq, self.ck, self.cv, self.A_log, self.dt_bias, Hl, 1, T)
+        mark('prologue')
         o, _ = chunk_gated_delta_rule(q, k, v, g, beta, use_qk_l2norm_in_kernel=True)
+        mark('gdn')
         self.launches = 2 + chunk_gated_delta_rule.launches
         o_seq = self._head_to_seq(o.reshape(T, Hl * D), Tl)
+        mark('head_to_seq')
         gate = x_local @ self.WgT
         y = rms_norm_gated(o_seq.reshape(Tl, self.H, D), gate.reshape(Tl, self.H, D), self.o_norm_w, self.eps)
-        return y.reshape(Tl, -1) @ self.WoT
+        out = y.reshape(Tl, -1) @ self.WoT
+        mark('epilogue')
+        return out
 
 
 class AttnMixer(_Ulysses):
@@ -219,8 +243,13 @@ class AttnMixer(_Ulysses):
             self._rope = rope_table(freqs_cis_3d(self.D, f, h, w), self.W.device)
         return self._rope
 
-    def __call__(self, x_local, events=None):
-        """``events`` (optional start/end pair) brackets the attention kernel."""
+    def __call__(self, x_local, events=None, phases=None):
+        """``events`` (optional start/end pair) brackets the attention kernel;
+        ``phases`` (optional list) receives (name, CUDA event) phase marks:
+        projection + norm/RoPE + seq->head exchange, attention, head->seq
+        exchange, o_proj."""
+        mark = _marker(phases, 'attn')
+        mark('start')
         Tl = x_local.shape[0]
         T = Tl * self.P
         Hl, D = self.Hl, self.D
@@ -238,9 +267,12 @@ class AttnMixer(_Ulysses):
                              ld=self.C, heads_per_block=Hl, block_stride=n * self.C)
 
         recv = self._project_exchange(x_local, self.W, self.b, norm_rope)  # [T, 3*Hl*D]
+        mark('proj_exchange')
         q, k, v = (recv[:, i * Hl * D:(i + 1) * Hl * D].reshape(1, T, Hl * D) for i in range(3))
         o = attention_fp8(q, k, v, Hl, events=events)
+        mark('attention')
         o_seq = self._head_to_seq(o.reshape(T, Hl * D), Tl)
-        if self.bo is None:
-            return o_seq @ self.WoT
-        return torch.addmm(self.bo, o_seq, self.WoT)
+        mark('head_to_seq')
+        out = o_seq @ self.WoT if self.bo is None else torch.addmm(self.bo, o_seq, self.WoT)
+        mark('o_proj')
+        return out

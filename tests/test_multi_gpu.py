@@ -1,7 +1,8 @@
 """Sequence-parallel paths on 2 GPUs (NCCL, one process per GPU): the hybrid
 block and a small DiT step sharded over two ranks must match the same model
-run on one GPU, and the DiT step captured as one CUDA graph (NCCL sends and
-receives inside) must match its eager run.  Skipped on boxes with fewer than
+run on one GPU, and the hybrid block and the DiT step captured as CUDA graphs
+(NCCL sends and receives inside) must match their eager runs; the graphs are
+destroyed before the process group on every rank.  Skipped on boxes with fewer than
 two GPUs.
 
 Tolerances: the sharded run changes only the GEMM shapes, the per-rank head
@@ -9,6 +10,8 @@ split of the GDN state pass (V-slice width, segment count) and the order of
 NCCL transfers, so the outputs agree to bf16 level: max-relative error
 <= 2e-2 and cosine similarity >= 0.9995.
 """
+import datetime
+import gc
 import os
 import socket
 
@@ -38,7 +41,8 @@ def _worker(rank, world, port, q):
     try:
         os.environ.update(MASTER_ADDR='127.0.0.1', MASTER_PORT=str(port))
         torch.cuda.set_device(rank)
-        dist.init_process_group('nccl', rank=rank, world_size=world, device_id=torch.device('cuda', rank))
+        dist.init_process_group('nccl', rank=rank, world_size=world, device_id=torch.device('cuda', rank),
+                                timeout=datetime.timedelta(seconds=120))
         from kairos_sensenova_b200.dit import DiTConfig, KairosDiT, make_weights
         from kairos_sensenova_b200.hybrid import HybridBlock
         res = {}
@@ -51,6 +55,13 @@ def _worker(rank, world, port, q):
             blk = HybridBlock(hid, H, 128, world=world, rank=rank, grid=(4, 32, 32))
             y = blk.forward(xf[rank * Tl:(rank + 1) * Tl].contiguous())
             res['hybrid'] = _cmp(y, ref[rank * Tl:(rank + 1) * Tl])
+            from kairos_sensenova_b200.graphs import GraphedStep
+            xg = xf[rank * Tl:(rank + 1) * Tl].contiguous()
+            gstep = GraphedStep(blk.forward, xg)       # NCCL sends/receives captured in the graph
+            yg = gstep(xg).clone()
+            torch.cuda.synchronize()
+            res['hybrid_graph'] = _cmp(yg, y)
+            del gstep                                  # graphs go before the process group does
             cfg = DiTConfig(dim=256, heads=2, ffn_dim=512, layers=4, text_dim=64, text_len=16, latent=(4, 16, 16))
             w = make_weights(cfg, 'cuda', seed=2)
             g2 = torch.Generator(device='cuda').manual_seed(7)
@@ -60,11 +71,14 @@ def _worker(rank, world, port, q):
             o1 = KairosDiT(cfg, weights=w)(lat, t, ctx)
             o2 = KairosDiT(cfg, world=world, rank=rank, weights=w)(lat, t, ctx)
             res['dit'] = _cmp(o2, o1)
-            from kairos_sensenova_b200.graphs import GraphedStep
             m2 = KairosDiT(cfg, world=world, rank=rank, weights=w)
-            o3 = GraphedStep(m2, lat, t, ctx)(lat, t, ctx)
+            dstep = GraphedStep(m2, lat, t, ctx)
+            o3 = dstep(lat, t, ctx).clone()
             torch.cuda.synchronize()
             res['dit_graph'] = _cmp(o3, o2)
+            del dstep
+        gc.collect()
+        torch.cuda.synchronize()
         dist.barrier()
         q.put((rank, res))
     except Exception as e:  # pragma: no cover - reported to the parent
