@@ -2,30 +2,29 @@
 // (tcgen05 + TMEM + TMA), sm_100a: e4m3 Q K^T, bf16 P V, fp32 accumulation.
 //
 // One CTA per (two 128-query tiles, batch*head); keys in tiles of BN = 128.
-//   warps 16, 18: TMA producers (Q once and K per key tile; V^T per key tile),
-//                 each into its own ring
-//   warps 17, 19: MMA issuers (one elected thread each, one per query tile t);
-//                 warp 17 also owns TMEM
-//                 S_t = Q_t K_j^T  -> TMEM S[t]   (kind::f8f6f4, e4m3, M128 N128 K32)
-//                 O_t += P_t V_j   -> TMEM O[t]   (kind::f16, bf16; A = P_t read
-//                                                  from TMEM, B = V^T from smem)
-//   warps 0..15 : softmax, four warpgroups (query tile t, key half): each thread
-//                 owns the 64 scores of one row in its key half (TMEM lane): S
-//                 from TMEM -> (running max only when a norm bound says it may
-//                 have grown; the two halves of a row then exchange their
-//                 maxima) -> P = 2^(s - m + SHIFT) in bf16, written back into the
-//                 first 32 of its 64 S columns -> final O / l -> bf16.
-// P aliases S: the probabilities of key tile j are packed (two bf16 per column)
-// into the first half of each key half's S columns, so S, P and O of both query
-// tiles fit the 512 TMEM columns with 128-key tiles.  Per query tile the chain is
-// QK(j) -> softmax(j) -> PV(j) -> QK(j+1), with QK(j+1) issued directly behind PV(j)
-// (tcgen05.mma operations of one thread execute in order, so PV(j) has read P before
-// QK(j+1) overwrites it).  The two query tiles take turns with their exponentials,
-// so one tile's softmax overlaps the other's matrix products on the tensor pipe.
+//   warp 16    : TMA producer (Q once; K and V^T per key tile, each into its own ring)
+//   warp 17    : MMA issuer (one elected thread, both query tiles) + TMEM owner
+//                S   = Q_t K_j^T  -> TMEM S    (kind::f8f6f4, e4m3, M128 N128 K32)
+//                O_t += P_t V_j   -> TMEM O[t] (kind::f16, bf16; A = P_t read from
+//                                               TMEM, B = V^T from shared memory)
+//   warps 0..15: softmax, four warpgroups (query tile t, key half): each thread
+//                owns the 64 scores of one row in its key half (TMEM lane).
+//
+// TMEM (512 columns): O_0 | O_1 | S | P_0 P_1.  The two query tiles share ONE score
+// buffer S: the softmax of tile t loads its 64 scores per row into registers and
+// releases S at once, so the product of the other tile (or of the next key tile)
+// is computed while the exponentials of this one run; the probabilities go to the
+// tile's own P columns (bf16 pairs).  The issuer's order per key tile j is
+//   QK_1(j) [S released by tile 0]  PV_1(j-1) [P_1 published]
+//   QK_0(j+1) [S released by tile 1]  PV_0(j) [P_0 published]
+// (tcgen05.mma operations of one thread execute in issue order), so the score
+// buffer alternates between the tiles and each tile's exponentials overlap the
+// other tile's products on the tensor pipe.  The softmax of tile t writes P_t(j)
+// only after PV_t(j-1) has completed (it has read P_t(j-1) and added into O_t).
 //
 // Every mbarrier wait is bounded; a wait that gives up records an error code in
 // the workspace and the CTA skips the rest of its work.  Before it exits, the
-// producers wait (bounded) for the last TMA load of every ring slot and each MMA
+// producer waits (bounded) for the last TMA load of every ring slot and the MMA
 // issuer for all of its MMAs (one final commit); only then is TMEM freed.  If
 // one of those drain waits gives up too, TMEM is left allocated rather than
 // freed under a running MMA.
@@ -37,7 +36,7 @@ namespace kb {
 namespace attn {
 
 constexpr int TC_BM = 128, TC_BN = 128, TC_D = 128;
-constexpr int TC_QT = 2;          // query tiles per CTA (ping-pong)
+constexpr int TC_QT = 2;          // query tiles per CTA
 constexpr float TC_SHIFT = 6.f;   // P = 2^(s - m + SHIFT)
 // Lazy-rescale threshold (log2 units): O and l are rescaled only when the
 // running max grows by more than TAU, so P <= 2^(SHIFT+TAU) = 2^46 and a row sum
@@ -46,14 +45,19 @@ constexpr float TC_SHIFT = 6.f;   // P = 2^(s - m + SHIFT)
 // give bounds ~15 log2 units above the first tile's max), so the exact row max is
 // rarely needed.
 constexpr float TC_TAU = 40.f;
-// Which score pairs of every 8 take the FMA-pipe polynomial instead of MUFU ex2
-// (one of four: measured best with the query tiles taking turns).
+// Whether the two query tiles' softmax groups take turns with their exponentials.
+#ifndef KB_ATTN_TURNS
+#define KB_ATTN_TURNS 0
+#endif
+// Which score pairs of every 4 take the FMA-pipe polynomial instead of MUFU ex2 (none
+// by default: with the shared score buffer the MUFU-only exponentials measured fastest,
+// 7.6 ms against 7.8 ms with one pair in four on the polynomial).
 #ifndef KB_ATTN_POLY_MASK
-#define KB_ATTN_POLY_MASK 0x1
+#define KB_ATTN_POLY_MASK 0x0
 #endif
 constexpr int TC_POLY_MASK = KB_ATTN_POLY_MASK;
-// TMEM columns: S_t (and P_t aliased into it) [128 t, 128 t + 128), O_t [256 + 128 t, +128).
-constexpr uint32_t TM_S = 0, TM_O = 256;
+// TMEM columns: O_t [128 t, 128 t + 128), S [256, 384), P_t [384 + 64 t, 384 + 64 t + 64).
+constexpr uint32_t TM_O = 0, TM_S = 256, TM_P = 384;
 
 struct TcSmem {
   static constexpr int KS = 4, VS = 3;
@@ -62,12 +66,12 @@ struct TcSmem {
   __nv_bfloat16 v[VS][2][TC_D * 64];            // bf16 v^T tiles: 2 atoms of 64 keys x 128 rows
   uint64_t q_full;
   uint64_t k_full[KS], k_empty[KS], v_full[VS], v_empty[VS];
-  uint64_t s_full[TC_QT], p_full[TC_QT], o_done[TC_QT];
-  // turn[t]: the other query tile finished its exponentials of a key tile.  The two
-  // softmax groups take turns (tile 0 key tile j, tile 1 key tile j, tile 0 key tile
-  // j + 1, ...), so one group's exponentials run while the other tile's products use
-  // the tensor pipe, instead of both contending for the MUFU unit at once.
-  uint64_t turn[TC_QT];
+  uint64_t s_full[TC_QT];    // S holds tile t's scores of the next key tile (MMA commit)
+  uint64_t s_free[TC_QT];    // tile t's softmax has loaded S (one arrival per warp)
+  uint64_t p_full[TC_QT];    // tile t's P (and any O rescale) is in TMEM (one arrival per warp)
+  uint64_t pv_done[TC_QT];   // PV_t of a key tile has completed (MMA commit)
+  uint64_t turn[TC_QT];      // optional: the other tile finished its exponentials
+  uint64_t o_done[TC_QT];
   uint64_t xbar[TC_QT][4];                      // per (tile, lane quarter): the two key halves of a row exchange a value
   float xch[TC_QT][2][2][TC_BM];                // [tile][use parity][half][row]
   uint64_t drain[TC_QT];
@@ -82,8 +86,8 @@ struct TcMaps {
 
 #ifdef KB_ATTN_TRACE
 __device__ long long* g_attn_trace;
-#define ATRACE(j, slot) do { if (g_attn_trace && blockIdx.x == 3 && blockIdx.y == 5 && (j) < 128) \
-  g_attn_trace[(j) * 16 + (slot)] = clock64(); } while (0)
+// the trace pointer is read once per thread (trp); a probe is one clock read and one store
+#define ATRACE(j, slot) do { if (trp && (threadIdx.x & 31) == 0 && (j) < 128) trp[(j) * 32 + (slot)] = clock64(); } while (0)
 #else
 #define ATRACE(j, slot) do { } while (0)
 #endif
@@ -98,13 +102,6 @@ KB_DEVI float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
-}
-
-
-KB_DEVI float fmax3(float a, float b, float c) {
-  float d;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-  return d;
 }
 
 // 2^x for a pair on the FMA pipe, to share the exponential load with the MUFU
@@ -127,10 +124,17 @@ KB_DEVI float2 exp2_poly2(float2 x) {
                      __int_as_float(__float_as_int(q.y) + (__float_as_int(t.y) << 23)));
 }
 
+// One arrival per warp: every lane's earlier tcgen05 loads/stores are ordered before
+// the arrival (fence, then warp barrier, then lane 0 arrives).
+KB_DEVI void warp_arrive_tc(uint64_t* bar, int lane) {
+  tc::tc_fence_before();
+  __syncwarp();
+  if (lane == 0) tc::mbar_arrive(bar);
+}
+
 // Block: warps 0-15 softmax (warp w: TMEM lane quarter w & 3, query tile (w >> 2) & 1,
-// key half w >> 3), warp 16 TMA producer of Q and K, warp 17 MMA issuer of tile 0 +
-// TMEM owner, warp 18 TMA producer of V^T, warp 19 MMA issuer of tile 1.
-constexpr int TC_THREADS = 640;
+// key half w >> 3), warp 16 TMA producer, warp 17 MMA issuer + TMEM owner.
+constexpr int TC_THREADS = 576;
 __global__ void __launch_bounds__(TC_THREADS, 1) attn_fp8_tc_kernel(const __grid_constant__ TcMaps maps, Params p,
                                                              int* err) {
   using SM = TcSmem;
@@ -147,19 +151,23 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_fp8_tc_kernel(const __grid
     tc::mbar_init(&sm.q_full, 1);
     for (int s = 0; s < KS; ++s) {
       tc::mbar_init(&sm.k_full[s], 1);
-      tc::mbar_init(&sm.k_empty[s], TC_QT);
+      tc::mbar_init(&sm.k_empty[s], 1);
     }
     for (int s = 0; s < VS; ++s) {
       tc::mbar_init(&sm.v_full[s], 1);
-      tc::mbar_init(&sm.v_empty[s], TC_QT);
+      tc::mbar_init(&sm.v_empty[s], 1);
     }
     for (int i = 0; i < TC_QT; ++i) {
       tc::mbar_init(&sm.s_full[i], 1);
-      tc::mbar_init(&sm.p_full[i], 256);
+      tc::mbar_init(&sm.s_free[i], 8);
+      tc::mbar_init(&sm.p_full[i], 8);
+      tc::mbar_init(&sm.pv_done[i], 1);
+      tc::mbar_init(&sm.turn[i], 8);
+      for (int w = 0; w < 4; ++w) tc::mbar_init(&sm.xbar[i][w], 64);
+    }
+    for (int i = 0; i < TC_QT; ++i) {
       tc::mbar_init(&sm.o_done[i], 1);
       tc::mbar_init(&sm.drain[i], 1);
-      tc::mbar_init(&sm.turn[i], 256);
-      for (int w = 0; w < 4; ++w) tc::mbar_init(&sm.xbar[i][w], 64);
     }
     sm.abort_flag = 0;
     sm.keep_tmem = 0;
@@ -174,95 +182,164 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_fp8_tc_kernel(const __grid
   tc::tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
   auto aborted = [&]() { return *((volatile int*)&sm.abort_flag) != 0; };
+#ifdef KB_ATTN_TRACE
+  long long* const trp = (blockIdx.x == 3 && blockIdx.y == 5) ? g_attn_trace : nullptr;
+#endif
 
   if (warp == 16) {
-    // ------------------------------------------------------------ TMA producer of Q and K
+    // ------------------------------------------------------------ TMA producer
+    // K(j) and V^T(j) in key-tile order; each ring slot is reused once the issuer's
+    // commit says every MMA reading it has completed.
     if (lane == 0) {
       tc::prefetch_tmap(&maps.q);
       tc::prefetch_tmap(&maps.k);
+      tc::prefetch_tmap(&maps.vt);
       tc::mbar_expect_tx(&sm.q_full, TC_QT * TC_BM * TC_D);
       for (int qt = 0; qt < TC_QT; ++qt)
         tc::tma_load_2d(sm.q[qt], &maps.q, &sm.q_full, 0, bh * p.S_pad + q0 + qt * TC_BM);
-      int issued = 0;
+      int kiss = 0, viss = 0;
       for (int j = 0; j < ntiles; ++j) {
-        const int st = j % KS, use = j / KS;
-        if (j >= KS && !tc::mbar_wait(&sm.k_empty[st], (use - 1) & 1)) { fail(sm, err, 11); break; }
+        const int st = j % KS, sv = j % VS;
+        if (j >= KS && !tc::mbar_wait(&sm.k_empty[st], (j / KS - 1) & 1)) { fail(sm, err, 11); break; }
         if (aborted()) break;
         tc::mbar_expect_tx(&sm.k_full[st], TC_BN * TC_D);
         tc::tma_load_2d(sm.k[st], &maps.k, &sm.k_full[st], 0, bh * p.S_pad + j * TC_BN);
-        ++issued;
+        ++kiss;
+        if (j >= VS && !tc::mbar_wait(&sm.v_empty[sv], (j / VS - 1) & 1)) { fail(sm, err, 16); break; }
+        if (aborted()) break;
+        tc::mbar_expect_tx(&sm.v_full[sv], 2 * TC_BN * TC_D);
+        tc::tma_load_2d(sm.v[sv][0], &maps.vt, &sm.v_full[sv], j * TC_BN, bh * TC_D);
+        tc::tma_load_2d(sm.v[sv][1], &maps.vt, &sm.v_full[sv], j * TC_BN + 64, bh * TC_D);
+        ++viss;
       }
       // before the CTA may exit, every load it issued must have landed
       bool drained = tc::mbar_wait(&sm.q_full, 0);
-      for (int j = issued > KS ? issued - KS : 0; j < issued; ++j)
+      for (int j = kiss > KS ? kiss - KS : 0; j < kiss; ++j)
         drained &= tc::mbar_wait(&sm.k_full[j % KS], (j / KS) & 1);
+      for (int j = viss > VS ? viss - VS : 0; j < viss; ++j)
+        drained &= tc::mbar_wait(&sm.v_full[j % VS], (j / VS) & 1);
       if (!drained) { fail(sm, err, 18); sm.keep_tmem = 1; }
     }
-  } else if (warp == 18) {
-    // ------------------------------------------------------------ TMA producer of V^T
-    if (lane == 0) {
-      tc::prefetch_tmap(&maps.vt);
-      int issued = 0;
-      for (int j = 0; j < ntiles; ++j) {
-        const int st = j % VS, use = j / VS;
-        if (j >= VS && !tc::mbar_wait(&sm.v_empty[st], (use - 1) & 1)) { fail(sm, err, 16); break; }
-        if (aborted()) break;
-        tc::mbar_expect_tx(&sm.v_full[st], 2 * TC_BN * TC_D);
-        tc::tma_load_2d(sm.v[st][0], &maps.vt, &sm.v_full[st], j * TC_BN, bh * TC_D);
-        tc::tma_load_2d(sm.v[st][1], &maps.vt, &sm.v_full[st], j * TC_BN + 64, bh * TC_D);
-        ++issued;
-      }
-      bool drained = true;
-      for (int j = issued > VS ? issued - VS : 0; j < issued; ++j)
-        drained &= tc::mbar_wait(&sm.v_full[j % VS], (j / VS) & 1);
-      if (!drained) { fail(sm, err, 19); sm.keep_tmem = 1; }
-    }
-  } else if (warp == 17 || warp == 19) {
-    // ------------------------------------------------------------ MMA issuers
-    // One thread per query tile: QK(j) once K_j landed, then PV(j) once the softmax
-    // published P(j).  s_full(j) tracks every earlier MMA of the thread, so when the
-    // softmax sees S(j), PV(j-1) has completed too (O may be rescaled).
-    if (lane == 0) {
-      const int qt = warp == 17 ? 0 : 1;
-      constexpr uint32_t IDESC_QK = tc::idesc_e4m3_f32(TC_BM, TC_BN);
-      constexpr uint32_t IDESC_PV = tc::idesc_bf16_f32(TC_BM, TC_D);
-      const uint32_t tS = tmem + TM_S + qt * 128, tO = tmem + TM_O + qt * TC_D;
-      const uint64_t dq = tc::sdesc_sw128_kmajor(sm.q[qt]);
-      bool ok = tc::mbar_wait(&sm.q_full, 0);
-      if (!ok) fail(sm, err, 12);
-      for (int j = 0; ok && j < ntiles; ++j) {
-        const int st = j % KS, sv = j % VS;
-        if (!tc::mbar_wait(&sm.k_full[st], (j / KS) & 1)) { fail(sm, err, 14); ok = false; break; }
-        if (aborted()) { ok = false; break; }
-        // QK(j) writes the S columns that PV(j-1) reads P from: tcgen05.mma operations
-        // of one thread execute in issue order, so it is issued right behind PV(j-1)
-        tc::tc_fence_after();
-        const uint64_t dk = tc::sdesc_sw128_kmajor(sm.k[st]);
+  } else if (warp == 17) {
+    // ------------------------------------------------------------ MMA issuer
+    // One issuer for both tiles, in the order QK_1(j), PV_1(j-1), QK_0(j+1), PV_0(j).
+    // The whole warp runs the schedule (waits, operand arithmetic) so every MMA operand
+    // is warp-uniform and stays in uniform registers; one elected lane issues each
+    // group of MMAs and its commits.
+    const bool leader = tc::elect_one();
+    constexpr uint32_t IDESC_QK = tc::idesc_e4m3_f32(TC_BM, TC_BN);
+    constexpr uint32_t IDESC_PV = tc::idesc_bf16_f32(TC_BM, TC_D);
+    const uint32_t tmem_u = __shfl_sync(0xffffffffu, tmem, 0);
+    const uint32_t tS = tmem_u + TM_S;
+    // descriptors of ring slot 0; slot s adds its byte offset >> 4
+    const uint64_t dq0 = tc::sdesc_sw128_kmajor(sm.q[0]);
+    const uint64_t dk0 = tc::sdesc_sw128_kmajor(sm.k[0]);
+    const uint64_t dv0 = tc::sdesc_sw128_kmajor(sm.v[0][0]);
+    auto commit = [&](uint64_t* bar) {
+      if (leader) tc::tc_commit(bar);
+      __syncwarp();
+    };
+    auto qk = [&](int t, int j) {   // S = Q_t K_j^T
+      const uint64_t dq = dq0 + (uint64_t)(t * (TC_BM * TC_D / 16));
+      const uint64_t dk = dk0 + (uint64_t)((j % KS) * (TC_BN * TC_D / 16));
+      if (leader) {
 #pragma unroll
         for (int ks = 0; ks < TC_D / 32; ++ks)
           tc::mma_f8f6f4(tS, dq + 2 * ks, dk + 2 * ks, IDESC_QK, ks > 0 ? 1u : 0u);
-        tc::tc_commit(&sm.s_full[qt]);
-        tc::tc_commit(&sm.k_empty[st]);
-        ATRACE(j, 0 + qt * 8);
-        if (!tc::mbar_wait(&sm.v_full[sv], (j / VS) & 1)) { fail(sm, err, 17); ok = false; break; }
-        if (!tc::mbar_wait(&sm.p_full[qt], j & 1)) { fail(sm, err, 13); ok = false; break; }
-        if (aborted()) { ok = false; break; }
-        tc::tc_fence_after();
-        // K = 16 keys per instruction: 8 TMEM columns of packed bf16 P (key half kh at
-        // columns 64 kh .. 64 kh + 31), 32 B of a V^T row in atom kh
-#pragma unroll
-        for (int ks = 0; ks < TC_BN / 16; ++ks) {
-          const int kh = ks >> 2;
-          const uint64_t dv = tc::sdesc_sw128_kmajor(sm.v[sv][kh]);
-          tc::mma_bf16_ts(tO, tS + kh * 64 + (ks & 3) * 8, dv + 2 * (ks & 3), IDESC_PV, (j > 0 || ks > 0) ? 1u : 0u);
-        }
-        tc::tc_commit(&sm.v_empty[sv]);
-        ATRACE(j, 1 + qt * 8);
+        tc::tc_commit(&sm.s_full[t]);
       }
-      if (ok) tc::tc_commit(&sm.o_done[qt]);
-      // every MMA this thread issued must complete before TMEM is freed
-      tc::tc_commit(&sm.drain[qt]);
-      if (!tc::mbar_wait(&sm.drain[qt], 0)) { fail(sm, err, 20); sm.keep_tmem = 1; }
+      __syncwarp();
+    };
+    auto pv = [&](int t, int j) {   // O_t += P_t V_j: K = 16 keys per instruction (8 P columns)
+      const uint32_t tO = tmem_u + TM_O + t * TC_D, tP = tmem_u + TM_P + t * 64;
+      const uint64_t dv = dv0 + (uint64_t)((j % VS) * (2 * TC_D * 64 * 2 / 16));
+      if (leader) {
+#pragma unroll
+        for (int ks = 0; ks < TC_BN / 16; ++ks)
+          tc::mma_bf16_ts(tO, tP + ks * 8, dv + (ks >> 2) * (TC_D * 64 * 2 / 16) + 2 * (ks & 3), IDESC_PV,
+                          (j > 0 || ks > 0) ? 1u : 0u);
+        tc::tc_commit(&sm.pv_done[t]);
+      }
+      __syncwarp();
+    };
+    // A probe of an mbarrier phase is issued before the current group of MMAs (its
+    // latency overlaps the issue); finish() only polls if that probe said no.
+    auto probe = [&](uint64_t* bar, uint32_t parity) { return tc::mbar_test_wait(bar, parity); };
+    auto finish = [&](uint64_t* bar, uint32_t parity, bool pre, int code) {
+      const bool w = __all_sync(0xffffffffu, pre || tc::mbar_test_wait_loop(bar, parity));
+      if (!w) fail(sm, err, code);
+      return w;
+    };
+    bool ok = __all_sync(0xffffffffu, tc::mbar_wait(&sm.q_full, 0) && tc::mbar_wait(&sm.k_full[0], 0));
+    if (!ok) fail(sm, err, 12);
+    if (ok) {
+      tc::tc_fence_after();
+      qk(0, 0);
+      ATRACE(0, 0);
+    }
+    bool pre_s0 = probe(&sm.s_free[0], 0);
+    for (int j = 0; ok && j < ntiles; ++j) {
+      const bool last = j + 1 == ntiles;
+      const int kn = (j + 1) % KS, vn = j % VS;
+      // QK_1(j): S is free once tile 0 has loaded its scores of key tile j
+      if (!finish(&sm.s_free[0], j & 1, pre_s0, 13) || aborted()) { ok = false; break; }
+      tc::tc_fence_after();
+      const bool pre_p1 = j >= 1 ? probe(&sm.p_full[1], (j - 1) & 1) : true;
+      qk(1, j);
+      commit(&sm.k_empty[j % KS]);   // both tiles' products with K_j issued
+      ATRACE(j, 1);
+      // PV_1(j-1)
+      bool pre_s1 = false, pre_k = true;
+      if (j >= 1) {
+        if (!finish(&sm.p_full[1], (j - 1) & 1, pre_p1, 14)) { ok = false; break; }
+        tc::tc_fence_after();
+        pre_s1 = probe(&sm.s_free[1], j & 1);
+        if (!last) pre_k = probe(&sm.k_full[kn], ((j + 1) / KS) & 1);
+        pv(1, j - 1);
+        commit(&sm.v_empty[(j - 1) % VS]);   // both tiles' products with V_{j-1} issued
+        ATRACE(j - 1, 3);
+      } else if (!last) {
+        pre_s1 = probe(&sm.s_free[1], j & 1);
+        pre_k = probe(&sm.k_full[kn], ((j + 1) / KS) & 1);
+      }
+      // QK_0(j+1): S is free once tile 1 has loaded its scores of key tile j
+      bool pre_p0, pre_v;
+      if (!last) {
+        if (!finish(&sm.k_full[kn], ((j + 1) / KS) & 1, pre_k, 15)) { ok = false; break; }
+        if (!finish(&sm.s_free[1], j & 1, pre_s1, 13)) { ok = false; break; }
+        tc::tc_fence_after();
+        pre_p0 = probe(&sm.p_full[0], j & 1);
+        pre_v = probe(&sm.v_full[vn], (j / VS) & 1);
+        qk(0, j + 1);
+        ATRACE(j + 1, 0);
+      } else {
+        pre_p0 = probe(&sm.p_full[0], j & 1);
+        pre_v = probe(&sm.v_full[vn], (j / VS) & 1);
+      }
+      // PV_0(j)
+      if (!finish(&sm.v_full[vn], (j / VS) & 1, pre_v, 17)) { ok = false; break; }
+      if (!finish(&sm.p_full[0], j & 1, pre_p0, 14)) { ok = false; break; }
+      tc::tc_fence_after();
+      pre_s0 = last ? true : probe(&sm.s_free[0], (j + 1) & 1);
+      pv(0, j);
+      ATRACE(j, 2);
+    }
+    if (ok) {   // PV_1 of the last key tile
+      const int j = ntiles - 1;
+      if (finish(&sm.p_full[1], j & 1, false, 14)) {
+        tc::tc_fence_after();
+        pv(1, j);
+        commit(&sm.v_empty[j % VS]);
+        ATRACE(j, 3);
+        commit(&sm.o_done[0]);
+        commit(&sm.o_done[1]);
+      }
+    }
+    // every MMA this warp issued must complete before TMEM is freed
+    commit(&sm.drain[0]);
+    if (!__all_sync(0xffffffffu, tc::mbar_wait(&sm.drain[0], 0))) {
+      fail(sm, err, 20);
+      sm.keep_tmem = 1;
     }
   } else {
     // ------------------------------------------------------------ softmax (warps 0..15)
@@ -270,14 +347,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_fp8_tc_kernel(const __grid
     const int half = warp >> 3;                      // key half: columns [64 half, 64 half + 64) of S
     const int r = (warp & 3) * 32 + lane;            // row in the tile == TMEM lane
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-    const uint32_t tS = tmem + TM_S + qt * 128 + half * 64 + lane_off,
-                   tO = tmem + TM_O + qt * TC_D + lane_off;
+    const uint32_t tS = tmem + TM_S + half * 64 + lane_off, tO = tmem + TM_O + qt * TC_D + lane_off,
+                   tP = tmem + TM_P + qt * 64 + half * 32 + lane_off;
     const float sq = scale_of(p.amax[(0 * p.B + b) * p.H + h]);
     const float sk = scale_of(p.amax[(1 * p.B + b) * p.H + h]);
     const float sl2 = sq * sk * p.softmax_scale * 1.4426950408889634f;   // raw score -> log2 units
     const float qb = 1.0625f * p.qn[(size_t)bh * p.S_pad + q0 + qt * TC_BM + r] + 0.012f;
     const float* knp = p.kn + (size_t)bh * (p.S_pad / 64);
     const int nk64 = p.S_pad / 64;
+    const bool tr = r == 0 && half == 0;
     float m_ref = -INFINITY, l = 0.f;
     float kn_next = fmaxf(knp[0], knp[min(1, nk64 - 1)]);   // key-norm bound of the coming 128-key tile
     int xuse = 0;
@@ -296,15 +374,23 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_fp8_tc_kernel(const __grid
       const float kn_j = kn_next;
       const int jn = min(j + 1, ntiles - 1);
       kn_next = fmaxf(knp[min(2 * jn, nk64 - 1)], knp[min(2 * jn + 1, nk64 - 1)]);
-      if (r == 0 && half == 0) ATRACE(j, 2 + qt * 8);
       if (!tc::mbar_wait(&sm.s_full[qt], j & 1)) { fail(sm, err, 21); ok = false; }
-      // my turn: tile 0 after tile 1 finished key tile j - 1, tile 1 after tile 0 finished j
-      if (qt == 0 ? j >= 1 : true)
-        if (!tc::mbar_wait(&sm.turn[qt], (qt == 0 ? j - 1 : j) & 1)) { fail(sm, err, 27); ok = false; }
-      if (r == 0 && half == 0) ATRACE(j, 3 + qt * 8);
+      if (tr) ATRACE(j, 8 + 4 * qt);
       if (__any_sync(0xffffffffu, !ok || aborted())) { ok = false; break; }
       tc::tc_fence_after();
+      // the row's 64 scores of this key half into registers; then S is released
+      uint32_t s[64];
+      tc::tmem_ld32(tS, s);
+      tc::tmem_ld32(tS + 32, s + 32);
+      tc::tmem_wait_ld();
+      warp_arrive_tc(&sm.s_free[qt], lane);
+      if (tr) ATRACE(j, 9 + 4 * qt);
       const int kvalid = p.S - j * TC_BN - half * 64;
+      if (kvalid < 64) {
+#pragma unroll
+        for (int c = 0; c < 64; ++c)
+          if (c >= kvalid) s[c] = __float_as_uint(-INFINITY);
+      }
       // Every score of this tile is at most |sl2| |q8_row| max|k8| (Cauchy-Schwarz on the
       // e4m3 vectors the MMA multiplies; the factors cover e4m3 rounding of the stored
       // unrounded norms and the fp32 accumulation).  While that bound stays within TAU
@@ -318,15 +404,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_fp8_tc_kernel(const __grid
       float alpha = 1.f;
       if (need_max) {
         float mpart = -INFINITY;
-#pragma unroll 1
-        for (int part = 0; part < 2; ++part) {
-          uint32_t s[32];
-          tc::tmem_ld32(tS + 32 * part, s);
-          tc::tmem_wait_ld();
 #pragma unroll
-          for (int c = 0; c < 32; ++c)
-            if (32 * part + c < kvalid) mpart = fmaxf(mpart, __uint_as_float(s[c]));
-        }
+        for (int c = 0; c < 64; ++c) mpart = fmaxf(mpart, __uint_as_float(s[c]));
         const float mraw = fmaxf(mpart, exchange(mpart));
         if (__any_sync(0xffffffffu, !ok)) break;
         const float m_new = fmaxf(m_ref, mraw * sl2);
@@ -336,62 +415,50 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_fp8_tc_kernel(const __grid
           l *= alpha;
         }
       }
-      // exponentials: P packed as bf16 pairs; scaling and row sums as f32x2.  The two
-      // 32-score parts are read before P overwrites the first of them.
+#if KB_ATTN_TURNS
+      if (qt == 0 ? j >= 1 : true)
+        if (!tc::mbar_wait(&sm.turn[qt], (qt == 0 ? j - 1 : j) & 1)) { fail(sm, err, 27); ok = false; }
+#endif
+      // exponentials: P packed as bf16 pairs (8 TMEM columns per 16 scores); scaling and
+      // row sums as f32x2
       const float bias = TC_SHIFT - m_ref;
       const float2 sl2v = make_float2(sl2, sl2), biasv = make_float2(bias, bias);
       float2 ls0 = make_float2(0.f, 0.f), ls1 = make_float2(0.f, 0.f);
+      uint32_t pk[32];
 #pragma unroll
-      for (int part = 0; part < 2; ++part) {
-        uint32_t pk[16];
-        uint32_t s[32];
-        tc::tmem_ld32(tS + 32 * part, s);
-        tc::tmem_wait_ld();
-        const int kv = kvalid - 32 * part;
-        if (kv < 32) {
-#pragma unroll
-          for (int c = 0; c < 32; ++c)
-            if (c >= kv) s[c] = __float_as_uint(-INFINITY);
-        }
-#pragma unroll
-        for (int c = 0; c < 32; c += 8) {
-          float2 x[4];
-#pragma unroll
-          for (int z = 0; z < 4; ++z)
-            x[z] = ffma2(make_float2(__uint_as_float(s[c + 2 * z]), __uint_as_float(s[c + 2 * z + 1])), sl2v, biasv);
-          float2 e[4];
-#pragma unroll
-          for (int z = 0; z < 4; ++z)
-            e[z] = ((TC_POLY_MASK >> z) & 1) ? exp2_poly2(x[z]) : make_float2(ex2(x[z].x), ex2(x[z].y));
-          ls0 = fadd2(ls0, fadd2(e[0], e[1]));
-          ls1 = fadd2(ls1, fadd2(e[2], e[3]));
-#pragma unroll
-          for (int z = 0; z < 4; ++z) pk[c / 2 + z] = pack_bf16(e[z].x, e[z].y);
-        }
-        // P of these 32 keys -> 16 columns at the start of the part-0 S columns (part 1's
-        // S columns, 32..63, are read before anything is written there)
-        tc::tmem_st16(tS + 16 * part, pk);
+      for (int z = 0; z < 32; ++z) {
+        const float2 x = ffma2(make_float2(__uint_as_float(s[2 * z]), __uint_as_float(s[2 * z + 1])), sl2v, biasv);
+        const float2 e = ((TC_POLY_MASK >> (z & 3)) & 1) ? exp2_poly2(x) : make_float2(ex2(x.x), ex2(x.y));
+        if (z & 1) ls1 = fadd2(ls1, e); else ls0 = fadd2(ls0, e);
+        pk[z] = pack_bf16(e.x, e.y);
       }
-      tc::mbar_arrive(&sm.turn[qt ^ 1]);   // the exponentials of this key tile are done
+#if KB_ATTN_TURNS
+      warp_arrive_tc(&sm.turn[qt ^ 1], lane);
+#endif
+      if (tr) ATRACE(j, 10 + 4 * qt);
       const float2 lsum = fadd2(ls0, ls1);
       l += lsum.x + lsum.y;
-      // O *= alpha before PV(j) adds into it (s_full(j) covers PV(j-1))
-      if (__any_sync(0xffffffffu, alpha != 1.f) && half == 0 && j >= 1) {
+      // P_t(j) overwrites P_t(j-1) and O_t may be rescaled: PV_t(j-1) must have completed
+      if (j >= 1 && !tc::mbar_wait(&sm.pv_done[qt], (j - 1) & 1)) { fail(sm, err, 22); ok = false; }
+      if (__any_sync(0xffffffffu, !ok)) break;
+      tc::tc_fence_after();
+      tc::tmem_st16(tP, pk);
+      tc::tmem_st16(tP + 16, pk + 16);
+      // O_t *= alpha before PV_t(j) adds into it; each key half rescales 64 of its columns
+      if (__any_sync(0xffffffffu, alpha != 1.f) && j >= 1) {
 #pragma unroll 1
-        for (int c = 0; c < TC_D / 32; ++c) {
+        for (int c = 0; c < 2; ++c) {
           uint32_t o[32];
-          tc::tmem_ld32(tO + c * 32, o);
+          tc::tmem_ld32(tO + half * 64 + c * 32, o);
           tc::tmem_wait_ld();
 #pragma unroll
           for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-          tc::tmem_st32(tO + c * 32, o);
+          tc::tmem_st32(tO + half * 64 + c * 32, o);
         }
       }
-      if (r == 0 && half == 0) ATRACE(j, 4 + qt * 8);
       tc::tmem_wait_st();
-      tc::tc_fence_before();
-      tc::mbar_arrive(&sm.p_full[qt]);
-      if (r == 0 && half == 0) ATRACE(j, 5 + qt * 8);
+      warp_arrive_tc(&sm.p_full[qt], lane);
+      if (tr) ATRACE(j, 11 + 4 * qt);
     }
     // epilogue: the row sum of both halves; each half writes 64 of the 128 output
     // columns once the last PV has completed

@@ -42,6 +42,25 @@ KB_DEVI bool mbar_wait(uint64_t* bar, uint32_t parity, long long budget = 400000
   return true;
 }
 
+// Non-blocking probe of a phase (no suspend), and a bounded polling loop over it.
+KB_DEVI bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+KB_DEVI bool mbar_test_wait_loop(uint64_t* bar, uint32_t parity, long long budget = 4000000000LL) {
+  if (mbar_test_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_test_wait(bar, parity)) {
+    if (clock64() - t0 > budget) return false;
+  }
+  return true;
+}
+
 // ------------------------------------------------------------------ TMA
 KB_DEVI void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
   asm volatile(
@@ -85,6 +104,12 @@ KB_DEVI void tmem_alloc(uint32_t* smem_dst, uint32_t ncols) {
 KB_DEVI void tmem_relinquish() { asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::); }
 KB_DEVI void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
   asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(taddr), "r"(ncols));
+}
+// One lane of the (fully active) warp is elected; the others get false.
+KB_DEVI bool elect_one() {
+  uint32_t r;
+  asm volatile("{\n .reg .pred p;\n elect.sync _|p, 0xffffffff;\n selp.u32 %0, 1, 0, p;\n}\n" : "=r"(r));
+  return r != 0;
 }
 KB_DEVI void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
 KB_DEVI void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
