@@ -96,13 +96,17 @@ KB_DEVI ChunkLoc locate(const TcParams& p, int c) {
 // of one CTA of each kernel, written to a buffer set by kb200_gdn_set_trace.
 #ifdef KB_GDN_TRACE
 __device__ long long* g_gdn_trace;
-#define PTRACE(slot) do { if (g_gdn_trace && blockIdx.x == 200 && blockIdx.y == 0 && threadIdx.x == 0) \
-  g_gdn_trace[(slot)] = clock64(); } while (0)
-#define STRACE(li, slot) do { if (g_gdn_trace && blockIdx.x == 0 && blockIdx.y == 0 && (li) < 256) \
-  g_gdn_trace[64 + (li) * 8 + (slot)] = clock64(); } while (0)
+// the buffer pointer is read once per thread (gtr, set at kernel entry); a probe is one
+// clock read and one store
+#define PTRACE(slot) do { if (gtr && blockIdx.x == 200 && blockIdx.y == 0 && threadIdx.x == 0) \
+  gtr[(slot)] = clock64(); } while (0)
+#define STRACE(li, slot) do { if (gtr && blockIdx.x == 0 && blockIdx.y == 0 && (li) < 256) \
+  gtr[64 + (li) * 8 + (slot)] = clock64(); } while (0)
+#define GTR_INIT long long* const gtr = g_gdn_trace
 #else
 #define PTRACE(slot) do { } while (0)
 #define STRACE(li, slot) do { } while (0)
+#define GTR_INIT do { } while (0)
 #endif
 
 KB_DEVI float bf(uint32_t u, int hi) { return hi ? __uint_as_float(u & 0xffff0000u) : __uint_as_float(u << 16); }
@@ -121,7 +125,8 @@ struct PrepLayout {
   static constexpr uint32_t T3 = 49152;        // A (fp32 [64][64], column-swizzled), then M rows
   static constexpr uint32_t T4 = 65536;        // D rows, then M^T rows, then (M^2)^T rows (fp32)
   static constexpr uint32_t VT = 81920;        // v tile, then beta v           [V/64 atoms][64][128 B]
-  static constexpr uint32_t MISC = VT + V * 128;
+  static constexpr uint32_t AQS = VT + V * 128;  // staging of the Aqk blob for its bulk store
+  static constexpr uint32_t MISC = AQS + 8192;
   static constexpr uint32_t BYTES = MISC + 640 + 1024;
   static constexpr uint32_t TMEM_COLS = (128 + V / 2) <= 256 ? 256 : 512;
 };
@@ -163,6 +168,7 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_tc_kernel(const __grid_consta
   float* As = reinterpret_cast<float*>(sm + LY::T3);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int c = blockIdx.x, h = blockIdx.y, H = p.H;
+  GTR_INIT;
   const ChunkLoc loc = locate(p, c);
   const int t0 = loc.bos + loc.it * BT, L = loc.len;
   if (L <= 0) return;
@@ -181,7 +187,14 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_tc_kernel(const __grid_consta
   __syncthreads();
   PTRACE(0);
   tc::tc_fence_after();
-  const uint32_t tmem = ms.tmem_base;
+  // warp-uniform TMEM base (broadcast from lane 0): MMA operands stay in uniform registers
+  const uint32_t tmem = __shfl_sync(0xffffffffu, ms.tmem_base, 0);
+  // shared-memory descriptors of every MMA operand tile, computed by every thread (warp-uniform)
+  const uint64_t d_kt = tc::sdesc_sw128_kmajor(sm + LY::KT), d_qt = tc::sdesc_sw128_kmajor(sm + LY::QT);
+  const uint64_t d_t2 = tc::sdesc_sw128_kmajor(sm + LY::T2), d_t3 = tc::sdesc_sw128_kmajor(sm + LY::T3);
+  const uint64_t d_t4 = tc::sdesc_sw128_kmajor(sm + LY::T4);
+  const uint64_t d_ai_mn = tc::sdesc_sw128_mnmajor(sm + LY::QT, 8192), d_kt_mn = tc::sdesc_sw128_mnmajor(sm + LY::KT, 8192);
+  const uint64_t d_vt_mn = tc::sdesc_sw128_mnmajor(sm + LY::VT, 8192);
   const uint32_t tq = tmem + ((uint32_t)(warp * 32) << 16);     // this warp's TMEM lane quarter
   const int r = warp * 16 + (lane & 15);                          // row of M = 64 products
   const int hc = lane >> 4;                                       // column half
@@ -263,21 +276,30 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_tc_kernel(const __grid_consta
 #pragma unroll
       for (int e = 0; e < 4; ++e) w[e] = pack_bf16(bf(w[e], 0) * rs, bf(w[e], 1) * rs);
       *reinterpret_cast<uint4*>(tile + (j >> 3) * 8192 + swz(rr, j & 7)) = x[j];
-      if (rr < L) *reinterpret_cast<uint4*>(dst + ((size_t)(t0 + rr) * H + h) * 128 + j * 8) = x[j];
+      // a partial chunk's tail rows belong to the next sequence: row stores there
+      if (L < BT && rr < L) *reinterpret_cast<uint4*>(dst + ((size_t)(t0 + rr) * H + h) * 128 + j * 8) = x[j];
     }
   }
   tc::fence_proxy_async_smem();
   __syncthreads();
+  if (ok && p.l2norm && L == BT && tid == 0) {
+    // a full chunk's normalised q and k tiles -> global by TMA (read back by the state pass)
+#pragma unroll
+    for (int a = 0; a < 2; ++a) {
+      tc::tma_store_3d(&maps.kn, sm + LY::KT + a * 8192, a * 64, h, t0);
+      tc::tma_store_3d(&maps.qn, sm + LY::QT + a * 8192, a * 64, h, t0);
+    }
+    tc::bulk_commit_group();
+  }
   // ---- S_kk = K K^T (TMEM cols 0..63), S_qk = Q K^T (cols 64..127) ----
-  if (ok && tid == 0) {
+  if (ok && warp == 0 && tc::elect_one()) {
     tc::tc_fence_after();
     constexpr uint32_t ID = tc::idesc_f32acc(1, 64, 64, 0, 0);
-    const uint64_t dk = tc::sdesc_sw128_kmajor(sm + LY::KT), dq = tc::sdesc_sw128_kmajor(sm + LY::QT);
 #pragma unroll
     for (int ks = 0; ks < 8; ++ks) {
       const uint32_t off = ((ks >> 2) * 8192 + (ks & 3) * 32) >> 4;
-      tc::mma_bf16(tmem + 0, dk + off, dk + off, ID, ks > 0);
-      tc::mma_bf16(tmem + 64, dq + off, dk + off, ID, ks > 0);
+      tc::mma_bf16(tmem + 0, d_kt + off, d_kt + off, ID, ks > 0);
+      tc::mma_bf16(tmem + 64, d_qt + off, d_kt + off, ID, ks > 0);
     }
     tc::tc_commit(&ms.mma_bar);
   }
@@ -299,8 +321,15 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_tc_kernel(const __grid_consta
     uint32_t sk[32], sq[32];
     tc::tmem_ld16x32bx2_x32<32>(tq + 0, sk);
     tc::tmem_ld16x32bx2_x32<32>(tq + 64, sq);
+    // the gate cumsums of this thread's 32 columns, loaded up front (the A scratch stores
+    // below would otherwise hold every later load behind them)
+    float gj[32];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 g4 = reinterpret_cast<const float4*>(ms.gcs)[8 * hc + i];
+      gj[4 * i] = g4.x; gj[4 * i + 1] = g4.y; gj[4 * i + 2] = g4.z; gj[4 * i + 3] = g4.w;
+    }
     tc::tmem_wait_ld();
-    unsigned char* ab = reinterpret_cast<unsigned char*>(p.ab) + ((size_t)c * H + h) * AQK_BYTES;
 #pragma unroll
     for (int c8 = 0; c8 < 4; ++c8) {
       uint32_t w[4];
@@ -311,16 +340,23 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_tc_kernel(const __grid_consta
         for (int q = 0; q < 2; ++q) {
           const int jj = c8 * 8 + e + q, j = 32 * hc + jj;
           // e^{g_r - g_j} where the causal masks keep the entry (j <= r)
-          const float fac = (rv && j <= r) ? __expf(gr - ms.gcs[j]) : 0.f;
+          const float fac = (rv && j <= r) ? __expf(gr - gj[jj]) : 0.f;
           f[q] = __uint_as_float(sq[jj]) * fac;
           As[as_idx(r, j)] = (j < r) ? br * fac * __uint_as_float(sk[jj]) : 0.f;   // A = beta_r e^{..} S_kk
         }
         w[e >> 1] = pack_bf16(f[0], f[1]);
       }
-      *reinterpret_cast<uint4*>(ab + swz(r, 4 * hc + c8)) = make_uint4(w[0], w[1], w[2], w[3]);
+      *reinterpret_cast<uint4*>(sm + LY::AQS + swz(r, 4 * hc + c8)) = make_uint4(w[0], w[1], w[2], w[3]);
     }
   }
+  tc::fence_proxy_async_smem();
+  // the q tile is overwritten next: the TMA store of the normalised q / k must have read it
+  if (tid == 0) tc::bulk_wait_group_read0();
   __syncthreads();
+  if (ok && tid == 0) {
+    tc::bulk_store(reinterpret_cast<unsigned char*>(p.ab) + ((size_t)c * H + h) * AQK_BYTES, sm + LY::AQS, AQK_BYTES);
+    tc::bulk_commit_group();
+  }
   PTRACE(3);
   // ---- Lo^T half-row r (column r of A below the diagonal blocks) -> T1; D^T row /
   // D row of the diagonal-block inverse (forward / back substitution, fp32) ----
@@ -374,8 +410,7 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_tc_kernel(const __grid_consta
   PTRACE(4);
   constexpr uint32_t ID_TF = tc::idesc_f32acc(2, 64, 64, 0, 0);   // tf32, both K-major
   // C[cols] = A B^T (M64 N64 K64, tf32): A rows [m][k], B rows [n][k], fp32, K-major
-  auto tf32_product = [&](uint32_t col, uint32_t a_off, uint32_t b_off) {
-    const uint64_t da = tc::sdesc_sw128_kmajor(sm + a_off), db = tc::sdesc_sw128_kmajor(sm + b_off);
+  auto tf32_product = [&](uint32_t col, uint64_t da, uint64_t db) {
 #pragma unroll
     for (int ks = 0; ks < 8; ++ks) {
       const uint32_t off = ((ks >> 2) * 8192 + (ks & 3) * 32) >> 4;
@@ -395,10 +430,10 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_tc_kernel(const __grid_consta
     for (int c8 = 0; c8 < 4; ++c8) st_f32x8(sm + off, r, 4 * hc + c8, v + 8 * c8);
   };
   // ---- round 1: M = Lo^T D^T -> cols 128..191, M^T = D Lo -> cols 192..255 ----
-  if (ok && tid == 0) {
+  if (ok && warp == 0 && tc::elect_one()) {
     tc::tc_fence_after();
-    tf32_product(128, LY::QT, LY::T4);
-    tf32_product(192, LY::T4, LY::QT);
+    tf32_product(128, d_qt, d_t4);
+    tf32_product(192, d_t4, d_qt);
     tc::tc_commit(&ms.mma_bar);
   }
   if (ok) mma_wait();
@@ -414,10 +449,10 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_tc_kernel(const __grid_consta
   tc::tc_fence_before();
   __syncthreads();
   // ---- round 2: Q = D^T M -> cols 128..191, (M^2)^T = M^T M^T -> cols 192..255 ----
-  if (ok && tid == 0) {
+  if (ok && warp == 0 && tc::elect_one()) {
     tc::tc_fence_after();
-    tf32_product(128, LY::T2, LY::T4);
-    tf32_product(192, LY::T4, LY::T3);
+    tf32_product(128, d_t2, d_t4);
+    tf32_product(192, d_t4, d_t3);
     tc::tc_commit(&ms.mma_bar);
   }
   if (ok) mma_wait();
@@ -439,9 +474,9 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_tc_kernel(const __grid_consta
   tc::tc_fence_before();
   __syncthreads();
   // ---- round 3: F = E M^2 -> cols 128..191 ----
-  if (ok && tid == 0) {
+  if (ok && warp == 0 && tc::elect_one()) {
     tc::tc_fence_after();
-    tf32_product(128, LY::QT, LY::T4);
+    tf32_product(128, d_qt, d_t4);
     tc::tc_commit(&ms.mma_bar);
   }
   if (ok) mma_wait();
@@ -458,33 +493,42 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_tc_kernel(const __grid_consta
         w[q] = pack_bf16(e[8 * c8 + 2 * q] + f[8 * c8 + 2 * q], e[8 * c8 + 2 * q + 1] + f[8 * c8 + 2 * q + 1]);
       *reinterpret_cast<uint4*>(sm + LY::QT + swz(r, 4 * hc + c8)) = make_uint4(w[0], w[1], w[2], w[3]);
     }
-    // k rows -> bf16(bf16(k beta) e^g) (wy_fast.py:77-79), v rows -> bf16(v beta) (:67), in place
+    // k rows -> bf16(bf16(k beta) e^g) (wy_fast.py:77-79), v rows -> bf16(v beta) (:67), in
+    // place; each thread loads its 8 chunks of a row first, then converts and stores them
+    // (the loads do not wait behind the stores)
     {
       const int rr = tid & 63, a = tid >> 6;
       const float b = ms.bs[rr], eg = __expf(ms.gcs[rr]);
       unsigned char* row = sm + LY::KT + a * 8192;
+      uint4 v4[8];
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) v4[ch] = *reinterpret_cast<const uint4*>(row + swz(rr, ch));
 #pragma unroll
       for (int ch = 0; ch < 8; ++ch) {
-        uint4 v4 = *reinterpret_cast<const uint4*>(row + swz(rr, ch));
-        uint32_t* w = reinterpret_cast<uint32_t*>(&v4);
+        uint32_t* w = reinterpret_cast<uint32_t*>(&v4[ch]);
 #pragma unroll
         for (int q = 0; q < 4; ++q)
           w[q] = pack_bf16(bf16_round(bf(w[q], 0) * b) * eg, bf16_round(bf(w[q], 1) * b) * eg);
-        *reinterpret_cast<uint4*>(row + swz(rr, ch)) = v4;
       }
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) *reinterpret_cast<uint4*>(row + swz(rr, ch)) = v4[ch];
     }
+#pragma unroll 1
     for (int job = tid; job < 64 * (V / 64); job += 128) {
       const int rr = job & 63, a = job >> 6;
       const float b = ms.bs[rr];
       unsigned char* row = sm + LY::VT + a * 8192;
+      uint4 v4[8];
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) v4[ch] = *reinterpret_cast<const uint4*>(row + swz(rr, ch));
 #pragma unroll
       for (int ch = 0; ch < 8; ++ch) {
-        uint4 v4 = *reinterpret_cast<const uint4*>(row + swz(rr, ch));
-        uint32_t* w = reinterpret_cast<uint32_t*>(&v4);
+        uint32_t* w = reinterpret_cast<uint32_t*>(&v4[ch]);
 #pragma unroll
         for (int q = 0; q < 4; ++q) w[q] = pack_bf16(bf(w[q], 0) * b, bf(w[q], 1) * b);
-        *reinterpret_cast<uint4*>(row + swz(rr, ch)) = v4;
       }
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) *reinterpret_cast<uint4*>(row + swz(rr, ch)) = v4[ch];
     }
   }
   tc::fence_proxy_async_smem();
@@ -492,17 +536,16 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_tc_kernel(const __grid_consta
   __syncthreads();
   // ---- w = Ai (beta e^g k) -> cols 0..127 (M64 N128); u^T = (beta v)^T Ai^T -> cols
   // 128 + 64 s (M128 N64 per 128-wide V slice s).  Ai^T rows are Ai's MN-major image. ----
-  if (ok && tid == 0) {
+  if (ok && warp == 0 && tc::elect_one()) {
     tc::tc_fence_after();
     constexpr uint32_t ID_W = tc::idesc_f32acc(1, 64, 128, 1, 1);
     constexpr uint32_t ID_U = tc::idesc_f32acc(1, 128, 64, 1, 1);
-    const uint64_t dai = tc::sdesc_sw128_mnmajor(sm + LY::QT, 8192);
-    const uint64_t dkt = tc::sdesc_sw128_mnmajor(sm + LY::KT, 8192);
+    const uint64_t dai = d_ai_mn, dkt = d_kt_mn;
 #pragma unroll
     for (int ks = 0; ks < 4; ++ks) tc::mma_bf16(tmem + 0, dai + ks * 128, dkt + ks * 128, ID_W, ks > 0);
 #pragma unroll
     for (int vs = 0; vs < V / 128; ++vs) {
-      const uint64_t dv = tc::sdesc_sw128_mnmajor(sm + LY::VT + vs * 16384, 8192);
+      const uint64_t dv = d_vt_mn + (uint64_t)(vs * 16384 / 16);
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks) tc::mma_bf16(tmem + 128 + 64 * vs, dv + ks * 128, dai + ks * 128, ID_U, ks > 0);
     }
@@ -512,7 +555,9 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_tc_kernel(const __grid_consta
   PTRACE(8);
   if (ok) {
     // w row r, columns 64 hc .. 64 hc + 63 -> W blob atom hc (bf16, 128-byte swizzle)
-    unsigned char* wb = reinterpret_cast<unsigned char*>(p.wb) + ((size_t)c * H + h) * W_BYTES + hc * 8192;
+    // W and U^T are staged in shared memory in their blob layout (T2, and T3 onwards: all
+    // free once the products completed) and leave by two bulk stores
+    unsigned char* wb = sm + LY::T2 + hc * 8192;
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
       uint32_t u[32];
@@ -530,7 +575,7 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_tc_kernel(const __grid_consta
     }
     // u^T row v = tid (M = 128: all lanes) -> U^T blob ([V rows][64 tokens] bf16 swizzled)
     const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
-    unsigned char* ub = reinterpret_cast<unsigned char*>(p.ub) + ((size_t)c * H + h) * (size_t)(V * 128);
+    unsigned char* ub = sm + LY::T3;
 #pragma unroll
     for (int vs = 0; vs < V / 128; ++vs) {
 #pragma unroll
@@ -550,8 +595,17 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_tc_kernel(const __grid_consta
       }
     }
   }
+  tc::fence_proxy_async_smem();
   tc::tc_fence_before();
   __syncthreads();
+  if (ok && tid == 0) {
+    tc::bulk_store(reinterpret_cast<unsigned char*>(p.wb) + ((size_t)c * H + h) * W_BYTES, sm + LY::T2, W_BYTES);
+    tc::bulk_store(reinterpret_cast<unsigned char*>(p.ub) + ((size_t)c * H + h) * (size_t)(V * 128), sm + LY::T3,
+                   V * 128);
+    tc::bulk_commit_group();
+  }
+  // shared memory stays allocated until every bulk store has read its source
+  if (tid == 0) tc::bulk_wait_group_read0();
   PTRACE(9);
   if (!ok && mma_uses > 0 && tid == 0) {
     // a wait gave up with MMAs issued: one more (bounded) wait for their completion
@@ -624,7 +678,8 @@ __device__ __noinline__ void emit_stage(unsigned char* __restrict__ ost_base, ui
     tc::tmem_wait_ld();
     if (half == 1) {
       tc::tc_fence_before();
-      tc::mbar_arrive(o_free);
+      __syncwarp();
+      if ((threadIdx.x & 31) == 0) tc::mbar_arrive(o_free);   // one arrival per output warp
     }
 #pragma unroll
     for (int u = 0; u < 16; ++u) {
@@ -657,6 +712,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_tc_kernel(const __gri
   StMisc& ms = *reinterpret_cast<StMisc*>(sm + LY::MISC);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, H = p.H;
   const int nseg = p.seg_mode ? p.nseg : 1;
+  GTR_INIT;
   const int nh = blockIdx.y / nseg, seg = blockIdx.y % nseg, n = nh / H, h = nh % H;
   const bool trans = p.seg_mode == 1 && (int)blockIdx.x >= V / 128;
   const int v0 = trans ? 0 : blockIdx.x * 128;
@@ -683,12 +739,12 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_tc_kernel(const __gri
       tc::mbar_init(&ms.in_full[s], 1);
       tc::mbar_init(&ms.in_empty[s], 1);
       tc::mbar_init(&ms.o_full[s], 1);
-      tc::mbar_init(&ms.o_free[s], 128);
+      tc::mbar_init(&ms.o_free[s], 4);
     }
     tc::mbar_init(&ms.p_full, 1);
     tc::mbar_init(&ms.x_full, 1);
-    tc::mbar_init(&ms.h_ready, 128);
-    tc::mbar_init(&ms.vg_ready, 128);
+    tc::mbar_init(&ms.h_ready, 4);    // one arrival per state warp
+    tc::mbar_init(&ms.vg_ready, 4);
     tc::mbar_init(&ms.drain, 1);
     ms.abort = 0;
     ms.keep_tmem = 0;
@@ -701,59 +757,75 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_tc_kernel(const __gri
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
-  const uint32_t tmem = ms.tmem_base;
+  // warp-uniform TMEM base (broadcast from lane 0): MMA operands stay in uniform registers
+  const uint32_t tmem = __shfl_sync(0xffffffffu, ms.tmem_base, 0);
   auto aborted = [&]() { return *((volatile int*)&ms.abort) != 0; };
 
   if (warp >= 8) {
-    if (warp == 8 && lane == 0) {
+    if (warp == 8) {
       // ---------------------------------------------------------------- MMA issuer
+      // The whole warp runs the schedule (bounded waits, operand arithmetic) so every MMA
+      // operand is warp-uniform and stays in uniform registers; one elected lane issues.
+      const bool leader = tc::elect_one();
       constexpr uint32_t ID_P = tc::idesc_f32acc(1, 128, 64, 0, 0);
       constexpr uint32_t ID_X = tc::idesc_f32acc(1, 128, 128, 0, 1);
       const uint64_t dh = tc::sdesc_sw128_kmajor(sm + LY::H);
       const uint64_t dvg = tc::sdesc_sw128_kmajor(sm + LY::VG), dvn = tc::sdesc_sw128_kmajor(sm + LY::VN);
+      const uint64_t dw0 = tc::sdesc_sw128_kmajor(sm + LY::W), dq0 = tc::sdesc_sw128_kmajor(sm + LY::Q);
+      const uint64_t dk0 = tc::sdesc_sw128_mnmajor(sm + LY::K, 8192), da0 = tc::sdesc_sw128_kmajor(sm + LY::A);
+      auto wait_all = [&](uint64_t* bar, uint32_t parity) {
+        return __all_sync(0xffffffffu, tc::mbar_test_wait_loop(bar, parity, WAIT_BUDGET));
+      };
       bool ok = true;
       for (int li = 0; li < nl && ok; ++li) {
         const int s = li & 1, b = li & 1;
-        unsigned char* st = sm + s * LY::STAGE;
+        const uint64_t so = (uint64_t)(s * (LY::STAGE / 16));   // stage offset in descriptor units
         // P = h^T W^T and O_inter = h^T Q^T once the state threads wrote h^T
-        ok = wait_(&ms.in_full[s], (li >> 1) & 1) && wait_(&ms.h_ready, li & 1) &&
-             (!out || li < 2 || wait_(&ms.o_free[b], ((li >> 1) - 1) & 1)) && !aborted();
-        if (!ok) { fail(p.err, 81); break; }
+        ok = wait_all(&ms.in_full[s], (li >> 1) & 1) && wait_all(&ms.h_ready, li & 1) &&
+             (!out || li < 2 || wait_all(&ms.o_free[b], ((li >> 1) - 1) & 1)) && !aborted();
+        if (!ok) { if (leader) fail(p.err, 81); break; }
         tc::tc_fence_after();
-        const uint64_t dw = tc::sdesc_sw128_kmajor(st + LY::W);
-#pragma unroll
-        for (int ks = 0; ks < 8; ++ks)
-          tc::mma_bf16(tmem + PCOL, dh + (((ks >> 2) * 16384 + (ks & 3) * 32) >> 4),
-                       dw + (((ks >> 2) * 8192 + (ks & 3) * 32) >> 4), ID_P, ks > 0);
-        tc::tc_commit(&ms.p_full);
-        if (out) {
-          const uint64_t dq = tc::sdesc_sw128_kmajor(st + LY::Q);
+        if (leader) {
 #pragma unroll
           for (int ks = 0; ks < 8; ++ks)
-            tc::mma_bf16(tmem + OICOL + 128 * b, dh + (((ks >> 2) * 16384 + (ks & 3) * 32) >> 4),
-                         dq + (((ks >> 2) * 8192 + (ks & 3) * 32) >> 4), ID_P, ks > 0);
+            tc::mma_bf16(tmem + PCOL, dh + (((ks >> 2) * 16384 + (ks & 3) * 32) >> 4),
+                         dw0 + so + (((ks >> 2) * 8192 + (ks & 3) * 32) >> 4), ID_P, ks > 0);
+          tc::tc_commit(&ms.p_full);
+          if (out) {
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks)
+              tc::mma_bf16(tmem + OICOL + 128 * b, dh + (((ks >> 2) * 16384 + (ks & 3) * 32) >> 4),
+                           dq0 + so + (((ks >> 2) * 8192 + (ks & 3) * 32) >> 4), ID_P, ks > 0);
+          }
         }
+        __syncwarp();
         // X = vg^T K (the state update) and O_intra = v_new^T Aqk^T once vg, v_new are written
-        ok = wait_(&ms.vg_ready, li & 1) && !aborted();
-        if (!ok) { fail(p.err, 82); break; }
+        ok = wait_all(&ms.vg_ready, li & 1) && !aborted();
+        if (!ok) { if (leader) fail(p.err, 82); break; }
         tc::tc_fence_after();
-        const uint64_t dk = tc::sdesc_sw128_mnmajor(st + LY::K, 8192);
+        if (leader) {
 #pragma unroll
-        for (int ks = 0; ks < 4; ++ks) tc::mma_bf16(tmem + XCOL, dvg + ks * 2, dk + ks * 128, ID_X, ks > 0);
-        tc::tc_commit(&ms.x_full);
-        if (out) {
-          const uint64_t da = tc::sdesc_sw128_kmajor(st + LY::A);
+          for (int ks = 0; ks < 4; ++ks) tc::mma_bf16(tmem + XCOL, dvg + ks * 2, dk0 + so + ks * 128, ID_X, ks > 0);
+          tc::tc_commit(&ms.x_full);
+          if (out) {
 #pragma unroll
-          for (int ks = 0; ks < 4; ++ks) tc::mma_bf16(tmem + OACOL + 128 * b, dvn + ks * 2, da + ks * 2, ID_P, ks > 0);
-          tc::tc_commit(&ms.o_full[b]);
+            for (int ks = 0; ks < 4; ++ks)
+              tc::mma_bf16(tmem + OACOL + 128 * b, dvn + ks * 2, da0 + so + ks * 2, ID_P, ks > 0);
+            tc::tc_commit(&ms.o_full[b]);
+          }
+          tc::tc_commit(&ms.in_empty[s]);
         }
-        tc::tc_commit(&ms.in_empty[s]);
-        STRACE(li, 5);
+        __syncwarp();
+        if (lane == 0) STRACE(li, 5);
       }
       if (!ok) ms.abort = 1;
       // every MMA issued here completes before TMEM is freed
-      tc::tc_commit(&ms.drain);
-      if (!wait_(&ms.drain, 0)) { fail(p.err, 72); ms.keep_tmem = 1; }
+      if (leader) tc::tc_commit(&ms.drain);
+      __syncwarp();
+      if (!wait_all(&ms.drain, 0)) {
+        if (leader) fail(p.err, 72);
+        ms.keep_tmem = 1;
+      }
     } else if (warp == 9 && lane == 0) {
       // ---------------------------------------------------------------- loads
       const uint32_t bytes = W_BYTES + 16384u + G_BYTES + (load_u ? 16384u : 0u) + (out ? 16384u + AQK_BYTES : 0u);
@@ -891,7 +963,8 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_tc_kernel(const __gri
       }
       tc::fence_proxy_async_smem();
       tc::tc_fence_before();
-      tc::mbar_arrive(&ms.h_ready);
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&ms.h_ready);
       if (tid == 0) STRACE(li, 2);
       // (b) v_new = u - h^T w^T (chunk_delta_h.py:142-163), gated by e^{g_last - g_t}
       ok = wait_(&ms.p_full, li & 1) && wait_(&ms.in_full[s], (li >> 1) & 1);
@@ -928,7 +1001,8 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_tc_kernel(const __gri
       if (out && v < 64) ms.eg[li & 3][v] = G[v];
       tc::fence_proxy_async_smem();
       tc::tc_fence_before();
-      tc::mbar_arrive(&ms.vg_ready);
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&ms.vg_ready);
       if (tid == 0) STRACE(li, 4);
     }
     if (ok && nl > 0) {
@@ -1042,6 +1116,12 @@ int launch_v(const KB200GdnArgs* a, const kb::gdntc::TcWs& L, char* ws, cudaStre
     if (int e = map3d(&pm.q, a->q, tokens, H, 128)) return e;
     if (int e = map3d(&pm.k, a->k, tokens, H, 128)) return e;
     if (int e = map3d(&pm.v, a->v, tokens, H, V)) return e;
+    pm.qn = pm.q;
+    pm.kn = pm.k;
+    if (a->use_qk_l2norm) {
+      if (int e = map3d(&pm.qn, p.qn, tokens, H, 128)) return e;
+      if (int e = map3d(&pm.kn, p.kn, tokens, H, 128)) return e;
+    }
     const size_t s1 = PrepLayout<V>::BYTES;
     cudaFuncSetAttribute(gdn_prep_tc_kernel<V>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s1);
     gdn_prep_tc_kernel<V><<<dim3(nchunks, H), 128, s1, st>>>(pm, p);

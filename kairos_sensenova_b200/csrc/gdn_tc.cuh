@@ -44,7 +44,7 @@ struct TcParams {
   float* seg_h;        // [N*H, nseg, 128, V]  segment start states
 };
 
-struct PrepMaps { CUtensorMap q, k, v; };
+struct PrepMaps { CUtensorMap q, k, v, qn, kn; };   // qn / kn: the l2-normalised copies (stores)
 struct StMaps { CUtensorMap q, k, o; };
 
 struct TcWs { size_t err, qn, kn, wb, ab, ub, gb, seg_b, seg_m, seg_h, total; int nseg, seg_chunks; };
