@@ -49,7 +49,7 @@ constexpr float TC_TAU = 40.f;
 #ifndef KB_ATTN_TURNS
 #define KB_ATTN_TURNS 0
 #endif
-// Which score pairs of every 4 take the FMA-pipe polynomial instead of MUFU ex2 (none
+// Which score pairs of every 8 take the FMA-pipe polynomial instead of MUFU ex2 (none
 // by default: with the shared score buffer the MUFU-only exponentials measured fastest,
 // 7.6 ms against 7.8 ms with one pair in four on the polynomial).
 #ifndef KB_ATTN_POLY_MASK
@@ -428,7 +428,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_fp8_tc_kernel(const __grid
 #pragma unroll
       for (int z = 0; z < 32; ++z) {
         const float2 x = ffma2(make_float2(__uint_as_float(s[2 * z]), __uint_as_float(s[2 * z + 1])), sl2v, biasv);
-        const float2 e = ((TC_POLY_MASK >> (z & 3)) & 1) ? exp2_poly2(x) : make_float2(ex2(x.x), ex2(x.y));
+        const float2 e = ((TC_POLY_MASK >> (z & 7)) & 1) ? exp2_poly2(x) : make_float2(ex2(x.x), ex2(x.y));
         if (z & 1) ls1 = fadd2(ls1, e); else ls0 = fadd2(ls0, e);
         pk[z] = pack_bf16(e.x, e.y);
       }
