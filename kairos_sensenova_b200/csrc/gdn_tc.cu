@@ -699,10 +699,11 @@ __device__ __noinline__ void emit_stage(unsigned char* __restrict__ ost_base, ui
 // TMEM columns of the state pass
 constexpr uint32_t XCOL = 0, PCOL = 128, OICOL = 192, OACOL = 256;   // O buffers at +128 b
 
-// Warps 0-3: the state chain; warps 4-7: the output of each chunk; warp 8: MMA
-// issuer; warp 9: loads.  (Twelve warps leave a thread 168 registers: the state
-// row takes 128 of them, so the chain reads TMEM 32 columns at a time.)
-constexpr int ST_THREADS = 384;
+// Warps 0-7: the state chain (warp w: TMEM lane quarter w & 3, rows k of the state
+// in half w >> 2); warps 8-11: the output of each chunk; warp 12: MMA issuer; warp
+// 13: loads.  Splitting each state column over two threads halves the TMEM reads
+// (and their latency) on the chain: a thread holds 64 state values.
+constexpr int ST_THREADS = 448;
 
 template <int V>
 __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_tc_kernel(const __grid_constant__ StMaps maps, TcParams p) {
@@ -743,8 +744,8 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_tc_kernel(const __gri
     }
     tc::mbar_init(&ms.p_full, 1);
     tc::mbar_init(&ms.x_full, 1);
-    tc::mbar_init(&ms.h_ready, 4);    // one arrival per state warp
-    tc::mbar_init(&ms.vg_ready, 4);
+    tc::mbar_init(&ms.h_ready, 8);    // one arrival per state warp
+    tc::mbar_init(&ms.vg_ready, 8);
     tc::mbar_init(&ms.drain, 1);
     ms.abort = 0;
     ms.keep_tmem = 0;
@@ -761,8 +762,8 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_tc_kernel(const __gri
   const uint32_t tmem = __shfl_sync(0xffffffffu, ms.tmem_base, 0);
   auto aborted = [&]() { return *((volatile int*)&ms.abort) != 0; };
 
-  if (warp >= 8) {
-    if (warp == 8) {
+  if (warp >= 12) {
+    if (warp == 12) {
       // ---------------------------------------------------------------- MMA issuer
       // The whole warp runs the schedule (bounded waits, operand arithmetic) so every MMA
       // operand is warp-uniform and stays in uniform registers; one elected lane issues.
@@ -826,7 +827,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_tc_kernel(const __gri
         if (leader) fail(p.err, 72);
         ms.keep_tmem = 1;
       }
-    } else if (warp == 9 && lane == 0) {
+    } else if (warp == 13 && lane == 0) {
       // ---------------------------------------------------------------- loads
       const uint32_t bytes = W_BYTES + 16384u + G_BYTES + (load_u ? 16384u : 0u) + (out ? 16384u + AQK_BYTES : 0u);
       int issued = 0;
@@ -863,11 +864,11 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_tc_kernel(const __gri
       for (int li = max(0, issued - 2); li < issued; ++li) drained &= wait_(&ms.in_full[li & 1], (li >> 1) & 1);
       if (!drained) { fail(p.err, 52); ms.keep_tmem = 1; }
     }
-  } else if (warp >= 4) {
+  } else if (warp >= 8) {
     // ------------------------------------------------------------------ output
     if (out) {
-      const int v = tid - 128;
-      const uint32_t tl = tmem + ((uint32_t)((warp - 4) * 32) << 16);
+      const int v = tid - 256;
+      const uint32_t tl = tmem + ((uint32_t)((warp - 8) * 32) << 16);
       // output of chunk lo: o = scale (e^{g_i} O_inter + O_intra), bf16, token rows of
       // this V slice
     const float scale = p.scale;
@@ -877,15 +878,15 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_tc_kernel(const __gri
       const int it = it0 + lo, L = min(BT, Tn - it * BT);
       const int t0 = bos + it * BT;
       // the previous chunk's TMA store must have finished reading the staging tile
-      if (tid == 128) tc::bulk_wait_group_read0();
+      if (tid == 256) tc::bulk_wait_group_read0();
       tc::bar_sync_named(2, 128);
-      if (tid == 128) STRACE(lo, 1);
+      if (tid == 256) STRACE(lo, 1);
       emit_stage(sm + LY::OST, tl + OICOL + 128 * b, tl + OACOL + 128 * b, ms.eg[lo & 3], scale, v, &ms.o_free[b]);
-      if (tid == 128) STRACE(lo, 7);
+      if (tid == 256) STRACE(lo, 7);
       tc::fence_proxy_async_smem();
       tc::bar_sync_named(2, 128);
       if (L == BT) {
-        if (tid == 128) {
+        if (tid == 256) {
           tc::tma_store_3d(&maps.o, sm + LY::OST, v0, h, t0);
           tc::tma_store_3d(&maps.o, sm + LY::OST + 8192, v0 + 64, h, t0);
           tc::bulk_commit_group();
@@ -909,16 +910,18 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_tc_kernel(const __gri
         tc::tc_fence_after();
         emit(lo);
       }
-      if (tid == 128) tc::bulk_wait_group0();   // the output stores complete before the CTA exits
+      if (tid == 256) tc::bulk_wait_group0();   // the output stores complete before the CTA exits
     }
   } else {
     // ------------------------------------------------------------------ state chain
-    const int v = tid;
-    const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
-    float hr[128];
+    // thread: state column v (TMEM lane v) and its rows k = 64 kh .. 64 kh + 63
+    const int v = tid & 127, kh = tid >> 7, k0 = 64 * kh;
+    const uint32_t tl = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    float hr[64];
     const bool seg_start0 = p.seg_mode != 0 && seg > 0;
 #pragma unroll
-    for (int k = 0; k < 128; ++k) {
+    for (int i = 0; i < 64; ++i) {
+      const int k = k0 + i;
       float init;
       if (trans)
         init = (k == v) ? 1.f : 0.f;
@@ -926,26 +929,25 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_tc_kernel(const __gri
         init = p.seg_mode == 2 ? p.seg_h[(((size_t)nh * nseg + seg) * 128 + k) * V + v0 + v] : 0.f;
       else
         init = p.h0 ? p.h0[((size_t)nh * 128 + k) * V + v0 + v] : 0.f;
-      hr[k] = init;
+      hr[i] = init;
     }
     float dec = 1.f;
     bool ok = true;
-    // h <- e^{g_last} h + X (the last chunk's state update), 64 columns per TMEM wait
+    // h <- e^{g_last} h + X (the last chunk's state update): this thread's 64 columns
+    // of X in one TMEM wait
     auto update_h = [&]() {
+      uint32_t xr[64];
+      tc::tmem_ld32(tl + XCOL + k0, xr);
+      tc::tmem_ld32(tl + XCOL + k0 + 32, xr + 32);
+      tc::tmem_wait_ld();
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        uint32_t xr[32];
-        tc::tmem_ld32(tl + XCOL + 32 * q, xr);
-        tc::tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) hr[32 * q + i] = fmaf(dec, hr[32 * q + i], __uint_as_float(xr[i]));
-      }
+      for (int i = 0; i < 64; ++i) hr[i] = fmaf(dec, hr[i], __uint_as_float(xr[i]));
     };
     for (int li = 0; li < nl; ++li) {
       const int s = li & 1;
       unsigned char* st = sm + s * LY::STAGE;
       if (tid == 0) STRACE(li, 0);
-      // (a) the previous chunk's update, then the bf16 h^T operand
+      // (a) the previous chunk's update, then this thread's half of the bf16 h^T operand
       if (li > 0) {
         ok = wait_(&ms.x_full, (li - 1) & 1);
         if (!__all_sync(0xffffffffu, ok) || aborted()) { ok = false; break; }
@@ -953,52 +955,52 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_tc_kernel(const __gri
         update_h();
       }
 #pragma unroll
-      for (int c16 = 0; c16 < 16; ++c16) {
+      for (int c8 = 0; c8 < 8; ++c8) {
         uint4 o;
-        o.x = pack_bf16(hr[8 * c16], hr[8 * c16 + 1]);
-        o.y = pack_bf16(hr[8 * c16 + 2], hr[8 * c16 + 3]);
-        o.z = pack_bf16(hr[8 * c16 + 4], hr[8 * c16 + 5]);
-        o.w = pack_bf16(hr[8 * c16 + 6], hr[8 * c16 + 7]);
-        *reinterpret_cast<uint4*>(sm + LY::H + (c16 >> 3) * 16384 + swz(v, c16 & 7)) = o;
+        o.x = pack_bf16(hr[8 * c8], hr[8 * c8 + 1]);
+        o.y = pack_bf16(hr[8 * c8 + 2], hr[8 * c8 + 3]);
+        o.z = pack_bf16(hr[8 * c8 + 4], hr[8 * c8 + 5]);
+        o.w = pack_bf16(hr[8 * c8 + 6], hr[8 * c8 + 7]);
+        *reinterpret_cast<uint4*>(sm + LY::H + kh * 16384 + swz(v, c8)) = o;
       }
       tc::fence_proxy_async_smem();
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&ms.h_ready);
       if (tid == 0) STRACE(li, 2);
-      // (b) v_new = u - h^T w^T (chunk_delta_h.py:142-163), gated by e^{g_last - g_t}
+      // (b) v_new = u - h^T w^T (chunk_delta_h.py:142-163), gated by e^{g_last - g_t};
+      // this thread: tokens 32 kh .. 32 kh + 31 of column v
       ok = wait_(&ms.p_full, li & 1) && wait_(&ms.in_full[s], (li >> 1) & 1);
       if (!__all_sync(0xffffffffu, ok) || aborted()) { ok = false; break; }
       tc::tc_fence_after();
       if (tid == 0) STRACE(li, 3);
       const float* G = ms.g[s];
+      {
+        uint32_t pr[32];
+        tc::tmem_ld32(tl + PCOL + 32 * kh, pr);
+        tc::tmem_wait_ld();
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-      uint32_t pr[32];
-      tc::tmem_ld32(tl + PCOL + 32 * half, pr);
-      tc::tmem_wait_ld();
+        for (int ch = 4 * kh; ch < 4 * kh + 4; ++ch) {
+          uint4 u4 = make_uint4(0, 0, 0, 0);
+          if (load_u) u4 = *reinterpret_cast<const uint4*>(st + LY::U + swz(v, ch));
+          const float4 f0 = reinterpret_cast<const float4*>(G + 64)[2 * ch];
+          const float4 f1 = reinterpret_cast<const float4*>(G + 64)[2 * ch + 1];
+          const float fg[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
+          const uint32_t uw[4] = {u4.x, u4.y, u4.z, u4.w};
+          uint32_t vnw[4], vgw[4];
 #pragma unroll
-      for (int ch = 4 * half; ch < 4 * half + 4; ++ch) {
-        uint4 u4 = make_uint4(0, 0, 0, 0);
-        if (load_u) u4 = *reinterpret_cast<const uint4*>(st + LY::U + swz(v, ch));
-        const float4 f0 = reinterpret_cast<const float4*>(G + 64)[2 * ch];
-        const float4 f1 = reinterpret_cast<const float4*>(G + 64)[2 * ch + 1];
-        const float fg[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
-        const uint32_t uw[4] = {u4.x, u4.y, u4.z, u4.w};
-        uint32_t vnw[4], vgw[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float a0 = bf(uw[q], 0) - __uint_as_float(pr[8 * (ch & 3) + 2 * q]);
-          const float a1 = bf(uw[q], 1) - __uint_as_float(pr[8 * (ch & 3) + 2 * q + 1]);
-          vnw[q] = pack_bf16(a0, a1);
-          vgw[q] = pack_bf16(a0 * fg[2 * q], a1 * fg[2 * q + 1]);
+          for (int q = 0; q < 4; ++q) {
+            const float a0 = bf(uw[q], 0) - __uint_as_float(pr[8 * (ch & 3) + 2 * q]);
+            const float a1 = bf(uw[q], 1) - __uint_as_float(pr[8 * (ch & 3) + 2 * q + 1]);
+            vnw[q] = pack_bf16(a0, a1);
+            vgw[q] = pack_bf16(a0 * fg[2 * q], a1 * fg[2 * q + 1]);
+          }
+          *reinterpret_cast<uint4*>(sm + LY::VN + swz(v, ch)) = make_uint4(vnw[0], vnw[1], vnw[2], vnw[3]);
+          *reinterpret_cast<uint4*>(sm + LY::VG + swz(v, ch)) = make_uint4(vgw[0], vgw[1], vgw[2], vgw[3]);
         }
-        *reinterpret_cast<uint4*>(sm + LY::VN + swz(v, ch)) = make_uint4(vnw[0], vnw[1], vnw[2], vnw[3]);
-        *reinterpret_cast<uint4*>(sm + LY::VG + swz(v, ch)) = make_uint4(vgw[0], vgw[1], vgw[2], vgw[3]);
-      }
       }
       dec = G[128];
-      if (out && v < 64) ms.eg[li & 3][v] = G[v];
+      if (out && tid < 64) ms.eg[li & 3][tid] = G[tid];
       tc::fence_proxy_async_smem();
       tc::tc_fence_before();
       __syncwarp();
@@ -1010,7 +1012,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_tc_kernel(const __gri
       tc::tc_fence_after();
       update_h();
     }
-    ok = tc::bar_red_and(1, 128, ok && !aborted());
+    ok = tc::bar_red_and(1, 256, ok && !aborted());
     if (!ok) {
       if (tid == 0) fail(p.err, 71);
       ms.abort = 1;
@@ -1022,13 +1024,14 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_tc_kernel(const __gri
         dst = p.ht + (size_t)nh * 128 * V;
       if (dst) {
         if (trans) {
-          // row v of the transposed transition (column v of M)
+          // row v of the transposed transition (column v of M), this thread's 64 entries
 #pragma unroll
-          for (int k = 0; k < 128; k += 4)
-            *reinterpret_cast<float4*>(dst + (size_t)v * 128 + k) = make_float4(hr[k], hr[k + 1], hr[k + 2], hr[k + 3]);
+          for (int i = 0; i < 64; i += 4)
+            *reinterpret_cast<float4*>(dst + (size_t)v * 128 + k0 + i) =
+                make_float4(hr[i], hr[i + 1], hr[i + 2], hr[i + 3]);
         } else {
 #pragma unroll
-          for (int k = 0; k < 128; ++k) dst[(size_t)k * V + v0 + v] = hr[k];
+          for (int i = 0; i < 64; ++i) dst[(size_t)(k0 + i) * V + v0 + v] = hr[i];
         }
       }
     }
