@@ -75,6 +75,20 @@ int kb200_gdn_launch_count(const KB200GdnArgs* a);
 /* Launch the forward.  `workspace` must be 256-byte aligned. */
 int kb200_gdn_chunk_fwd(const KB200GdnArgs* a, void* workspace, size_t workspace_bytes,
                         void* stream);
+/* Sliding-window attention: query i attends keys i - window_left .. i + window_right
+ * (a negative bound means unbounded), the window_size = (left, right) of the
+ * reference's flash_attention call (kairos/modules/dits/kairos_dit.py:232-277, used by
+ * SelfAttention with window_size / dilated_length, :423-507).  Key tiles entirely
+ * outside the window of a 256-query block are skipped.  Same other arguments as
+ * kb200_attn_fp8_fwd / _attend; _attend_window follows a _quantize. */
+int kb200_attn_fp8_fwd_window(const void* q, const void* k, const void* v, void* o, int64_t B,
+                              int64_t S, int64_t H, int64_t D, int64_t row_stride, float softmax_scale,
+                              void* workspace, size_t workspace_bytes, void* stream, int64_t window_left,
+                              int64_t window_right);
+int kb200_attn_fp8_attend_window(const void* q, const void* k, const void* v, void* o, int64_t B,
+                                 int64_t S, int64_t H, int64_t D, int64_t row_stride, float softmax_scale,
+                                 void* workspace, size_t workspace_bytes, void* stream, int64_t window_left,
+                                 int64_t window_right);
 /* Synchronises `stream` and reports KB200_ERR_TIMEOUT if a bounded device-side
  * wait of the last kb200_gdn_chunk_fwd on `workspace` gave up (the kernels then
  * record the site, let their copies in flight land and stop instead of hanging;

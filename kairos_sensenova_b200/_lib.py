@@ -74,6 +74,8 @@ SIGNATURES = {
     'kb200_attn_fp8_fwd': _ATTN_SIG,
     'kb200_attn_fp8_quantize': _ATTN_SIG,
     'kb200_attn_fp8_attend': _ATTN_SIG,
+    'kb200_attn_fp8_fwd_window': (_ATTN_SIG[0], _ATTN_SIG[1] + [ctypes.c_int64] * 2),
+    'kb200_attn_fp8_attend_window': (_ATTN_SIG[0], _ATTN_SIG[1] + [ctypes.c_int64] * 2),
     'kb200_attn_fp8_status': (ctypes.c_int, [ctypes.c_void_p] + [ctypes.c_int64] * 3 + [ctypes.c_void_p]),
     'kb200_gdn_prologue': (ctypes.c_int, [ctypes.POINTER(GdnPrologueArgs), ctypes.c_void_p]),
     'kb200_rmsnorm_gated': (ctypes.c_int, [ctypes.c_void_p] * 4 + [ctypes.c_int64] * 4 +

@@ -9,8 +9,11 @@ accumulation; the P.V half runs on bf16 probabilities and the bf16 V (with P
 and V in e4m3 too, the cosine similarity to the bf16 reference would sit near
 0.9986 on N(0,1) data, below the 0.999 contract; this way it is ~0.9992).  Like the reference's
 quantised backends (``SageAttention3Module``, ``kairos_dit.py:398-420``) it
-raises ``NotImplementedError`` for an ``attn_mask``; it also raises for a
-sliding ``window_size``, which it does not implement.
+raises ``NotImplementedError`` for an ``attn_mask``.  A sliding ``window_size``
+(left, right) restricts query i to keys i - left .. i + right, as the reference's
+flash-attention call does for ``SelfAttention`` (``kairos_dit.py:423-507``; its
+dilation is a rearrangement before this call); key tiles outside every window of a
+256-query block are skipped.
 """
 from __future__ import annotations
 
@@ -22,11 +25,13 @@ from . import _lib
 
 def attention_fp8(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, num_heads: int,
                   softmax_scale: float | None = None,
-                  events=None, check: bool = False) -> torch.Tensor:
+                  events=None, check: bool = False, window_size=(-1, -1)) -> torch.Tensor:
     """q, k, v: [B, S, H*D] (bf16; other float dtypes are converted) -> [B, S, H*D] bf16.
 
     ``events``: optional (start, end) CUDA events recorded on the launch stream
-    around the attention kernel alone (after quantisation)."""
+    around the attention kernel alone (after quantisation).  ``window_size``:
+    (left, right) sliding window as in flash-attention (query i sees keys
+    i - left .. i + right; -1 = unbounded)."""
     if q.device.type != 'cuda':
         raise RuntimeError('attention_fp8: inputs must be CUDA tensors (no CPU path)')
     if q.dim() != 3 or k.shape != q.shape or v.shape != q.shape:
@@ -56,12 +61,20 @@ def attention_fp8(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, num_heads: 
         stream = torch.cuda.current_stream(dev).cuda_stream
         args = (qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), o.data_ptr(), B, S, num_heads, D, ld,
                 float(softmax_scale), ws.data_ptr(), nbytes, stream)
+        wl, wr = (int(x) for x in window_size)
+        windowed = wl >= 0 or wr >= 0
         if events is None:
-            _lib.check(L.kb200_attn_fp8_fwd(*args), 'attention_fp8')
+            if windowed:
+                _lib.check(L.kb200_attn_fp8_fwd_window(*args, wl, wr), 'attention_fp8')
+            else:
+                _lib.check(L.kb200_attn_fp8_fwd(*args), 'attention_fp8')
         else:
             _lib.check(L.kb200_attn_fp8_quantize(*args), 'attention_fp8 quantize')
             events[0].record()
-            _lib.check(L.kb200_attn_fp8_attend(*args), 'attention_fp8 attend')
+            if windowed:
+                _lib.check(L.kb200_attn_fp8_attend_window(*args, wl, wr), 'attention_fp8 attend')
+            else:
+                _lib.check(L.kb200_attn_fp8_attend(*args), 'attention_fp8 attend')
             events[1].record()
         if check:   # synchronises; raises if a bounded device wait gave up
             _lib.check(L.kb200_attn_fp8_status(ws.data_ptr(), B, S, num_heads, stream),
@@ -79,9 +92,7 @@ class AttentionModule(nn.Module):
     def forward(self, q, k, v, attn_mask=None, window_size=(-1, -1)):
         if attn_mask is not None:
             raise NotImplementedError('FP8 attention path does not support arbitrary attn_mask')
-        if tuple(window_size) != (-1, -1):
-            raise NotImplementedError('FP8 attention path does not implement windowed attention')
-        return attention_fp8(q, k, v, self.num_heads)
+        return attention_fp8(q, k, v, self.num_heads, window_size=window_size)
 
 
 FP8AttentionModule = AttentionModule

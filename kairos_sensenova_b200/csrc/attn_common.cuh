@@ -21,6 +21,7 @@ struct Params {
   int B, S, H, S_pad;
   int64_t ld;    // elements between consecutive tokens of q/k/v (H*D when contiguous)
   float softmax_scale;
+  int win_left, win_right;   // sliding window (query i sees keys i - left .. i + right); -1: unbounded
   long long* trace;  // optional event timestamps of CTA (0,0) (builds with KB_ATTN_TRACE only)
 };
 

@@ -208,6 +208,7 @@ int attn_setup(attn::Params& p, AttnWs& w, const void* q, const void* k, const v
   p.S_pad = w.S_pad;
   p.ld = row_stride;
   p.softmax_scale = softmax_scale;
+  p.win_left = p.win_right = -1;   // no window
   return KB200_OK;
 }
 
@@ -250,6 +251,31 @@ extern "C" int kb200_attn_fp8_quantize(KB_ATTN_ARGS) {
 
 extern "C" int kb200_attn_fp8_attend(KB_ATTN_ARGS) {
   KB_ATTN_SETUP
+  return attn_attend(p, w, st);
+}
+
+// Sliding-window variants: query i attends keys i - window_left .. i + window_right
+// (a negative bound is unbounded), flash-attention's window_size semantics.
+namespace {
+int set_window(attn::Params& p, int64_t window_left, int64_t window_right) {
+  if (window_left > INT32_MAX || window_right > INT32_MAX)
+    return set_error(KB200_ERR_INVALID, "attn_fp8: window bound too large");
+  p.win_left = window_left < 0 ? -1 : (int)window_left;
+  p.win_right = window_right < 0 ? -1 : (int)window_right;
+  return KB200_OK;
+}
+}  // namespace
+
+extern "C" int kb200_attn_fp8_fwd_window(KB_ATTN_ARGS, int64_t window_left, int64_t window_right) {
+  KB_ATTN_SETUP
+  if (int e = set_window(p, window_left, window_right)) return e;
+  if (int e = attn_quantize(p, w, st)) return e;
+  return attn_attend(p, w, st);
+}
+
+extern "C" int kb200_attn_fp8_attend_window(KB_ATTN_ARGS, int64_t window_left, int64_t window_right) {
+  KB_ATTN_SETUP
+  if (int e = set_window(p, window_left, window_right)) return e;
   return attn_attend(p, w, st);
 }
 

@@ -145,7 +145,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_fp8_tc_kernel(const __grid
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
   const int q0 = blockIdx.x * (TC_QT * TC_BM);
-  const int ntiles = (p.S + TC_BN - 1) / TC_BN;
+  // key tiles this CTA visits: all of them, or those a sliding window (flash-attention's
+  // window_size = (left, right): query i sees keys i - left .. i + right) reaches from
+  // its 256 queries.  Loop indices below count from j_lo.
+  int j_lo = 0, j_hi = (p.S + TC_BN - 1) / TC_BN;
+  if (p.win_left >= 0) j_lo = max(0, q0 - p.win_left) / TC_BN;
+  if (p.win_right >= 0) j_hi = min(j_hi, (q0 + TC_QT * TC_BM - 1 + p.win_right) / TC_BN + 1);
+  const int ntiles = j_hi - j_lo;
 
   if (tid == 0) {
     tc::mbar_init(&sm.q_full, 1);
@@ -203,13 +209,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_fp8_tc_kernel(const __grid
         if (j >= KS && !tc::mbar_wait(&sm.k_empty[st], (j / KS - 1) & 1)) { fail(sm, err, 11); break; }
         if (aborted()) break;
         tc::mbar_expect_tx(&sm.k_full[st], TC_BN * TC_D);
-        tc::tma_load_2d(sm.k[st], &maps.k, &sm.k_full[st], 0, bh * p.S_pad + j * TC_BN);
+        tc::tma_load_2d(sm.k[st], &maps.k, &sm.k_full[st], 0, bh * p.S_pad + (j_lo + j) * TC_BN);
         ++kiss;
         if (j >= VS && !tc::mbar_wait(&sm.v_empty[sv], (j / VS - 1) & 1)) { fail(sm, err, 16); break; }
         if (aborted()) break;
         tc::mbar_expect_tx(&sm.v_full[sv], 2 * TC_BN * TC_D);
-        tc::tma_load_2d(sm.v[sv][0], &maps.vt, &sm.v_full[sv], j * TC_BN, bh * TC_D);
-        tc::tma_load_2d(sm.v[sv][1], &maps.vt, &sm.v_full[sv], j * TC_BN + 64, bh * TC_D);
+        tc::tma_load_2d(sm.v[sv][0], &maps.vt, &sm.v_full[sv], (j_lo + j) * TC_BN, bh * TC_D);
+        tc::tma_load_2d(sm.v[sv][1], &maps.vt, &sm.v_full[sv], (j_lo + j) * TC_BN + 64, bh * TC_D);
         ++viss;
       }
       // before the CTA may exit, every load it issued must have landed
@@ -357,7 +363,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_fp8_tc_kernel(const __grid
     const int nk64 = p.S_pad / 64;
     const bool tr = r == 0 && half == 0;
     float m_ref = -INFINITY, l = 0.f;
-    float kn_next = fmaxf(knp[0], knp[min(1, nk64 - 1)]);   // key-norm bound of the coming 128-key tile
+    // key-norm bound of the coming 128-key tile
+    float kn_next = fmaxf(knp[min(2 * j_lo, nk64 - 1)], knp[min(2 * j_lo + 1, nk64 - 1)]);
+    const int row_i = q0 + qt * TC_BM + r;   // this row's query index
     int xuse = 0;
     bool ok = true;
     uint64_t* xb = &sm.xbar[qt][warp & 3];
@@ -372,7 +380,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_fp8_tc_kernel(const __grid
     };
     for (int j = 0; j < ntiles; ++j) {
       const float kn_j = kn_next;
-      const int jn = min(j + 1, ntiles - 1);
+      const int jn = j_lo + min(j + 1, ntiles - 1);
       kn_next = fmaxf(knp[min(2 * jn, nk64 - 1)], knp[min(2 * jn + 1, nk64 - 1)]);
       if (!tc::mbar_wait(&sm.s_full[qt], j & 1)) { fail(sm, err, 21); ok = false; }
       if (tr) ATRACE(j, 8 + 4 * qt);
@@ -385,11 +393,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_fp8_tc_kernel(const __grid
       tc::tmem_wait_ld();
       warp_arrive_tc(&sm.s_free[qt], lane);
       if (tr) ATRACE(j, 9 + 4 * qt);
-      const int kvalid = p.S - j * TC_BN - half * 64;
-      if (kvalid < 64) {
+      // keys outside the sequence, or outside this row's window, score -inf
+      const int kb = (j_lo + j) * TC_BN + half * 64;
+      int c_lo = 0, c_hi = min(64, p.S - kb);
+      if (p.win_left >= 0) c_lo = max(c_lo, row_i - p.win_left - kb);
+      if (p.win_right >= 0) c_hi = min(c_hi, row_i + p.win_right - kb + 1);
+      if (c_lo > 0 || c_hi < 64) {
 #pragma unroll
         for (int c = 0; c < 64; ++c)
-          if (c >= kvalid) s[c] = __float_as_uint(-INFINITY);
+          if (c < c_lo || c >= c_hi) s[c] = __float_as_uint(-INFINITY);
       }
       // Every score of this tile is at most |sl2| |q8_row| max|k8| (Cauchy-Schwarz on the
       // e4m3 vectors the MMA multiplies; the factors cover e4m3 rounding of the stored
@@ -409,8 +421,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_fp8_tc_kernel(const __grid
         const float mraw = fmaxf(mpart, exchange(mpart));
         if (__any_sync(0xffffffffu, !ok)) break;
         const float m_new = fmaxf(m_ref, mraw * sl2);
-        if (__any_sync(0xffffffffu, m_new > m_ref + TC_TAU)) {
-          alpha = ex2(m_ref - m_new);                // 0 on the first tile
+        // the warp rescales together; a row that has seen no key yet (all of its scores
+        // so far masked by a window) keeps m = -inf
+        if (__any_sync(0xffffffffu, m_new > m_ref + TC_TAU) && m_new != -INFINITY) {
+          alpha = ex2(m_ref - m_new);                // 0 on the row's first seen key tile
           m_ref = m_new;
           l *= alpha;
         }
@@ -421,7 +435,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) attn_fp8_tc_kernel(const __grid
 #endif
       // exponentials: P packed as bf16 pairs (8 TMEM columns per 16 scores); scaling and
       // row sums as f32x2
-      const float bias = TC_SHIFT - m_ref;
+      // (no score of this row seen yet: every score here is -inf, and so is x)
+      const float bias = m_ref == -INFINITY ? 0.f : TC_SHIFT - m_ref;
       const float2 sl2v = make_float2(sl2, sl2), biasv = make_float2(bias, bias);
       float2 ls0 = make_float2(0.f, 0.f), ls1 = make_float2(0.f, 0.f);
       uint32_t pk[32];

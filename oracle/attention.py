@@ -29,6 +29,26 @@ def sdpa_reference(q, k, v, num_heads):
     return o.transpose(1, 2).reshape(B, S, HD)
 
 
+def sdpa_window_reference(q, k, v, num_heads, window_size):
+    """Windowed attention (flash-attention window_size semantics, equal lengths):
+    query i sees keys i - left .. i + right, -1 = unbounded; fp32 on CPU
+    (the reference's flash_attention call with window_size, ``kairos_dit.py:232-277``,
+    as SelfAttention issues it, ``:423-507``)."""
+    B, S, HD = q.shape
+    D = HD // num_heads
+    left, right = window_size
+    i = torch.arange(S)[:, None]
+    j = torch.arange(S)[None, :]
+    allow = torch.ones(S, S, dtype=torch.bool)
+    if left >= 0:
+        allow &= j >= i - left
+    if right >= 0:
+        allow &= j <= i + right
+    f = lambda x: x.float().reshape(B, S, num_heads, D).transpose(1, 2)  # noqa: E731
+    o = F.scaled_dot_product_attention(f(q), f(k), f(v), attn_mask=allow)
+    return o.transpose(1, 2).reshape(B, S, HD)
+
+
 def _e4m3(x):
     return x.clamp(-E4M3_MAX, E4M3_MAX).to(torch.float8_e4m3fn).float()
 

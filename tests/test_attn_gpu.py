@@ -82,3 +82,38 @@ def test_attn_fp8_strided_qkv_views_match_contiguous():
     o1 = attention_fp8(q, k, v, H)
     o2 = attention_fp8(q.contiguous(), k.contiguous(), v.contiguous(), H)
     assert torch.equal(o1, o2)
+
+
+@pytest.mark.parametrize('S,H,window', [(1000, 2, (64, 64)), (777, 3, (0, 300)), (4096, 2, (300, 10)),
+                                        (2000, 2, (-1, 5)), (3000, 2, (100, -1)), (300, 2, (3, 3))])
+def test_attn_fp8_sliding_window_vs_oracle(S, H, window):
+    """flash-attention window_size semantics: query i attends keys i - left .. i + right
+    (the reference's SelfAttention, kairos_dit.py:423-507, calls attention that way)."""
+    from kairos_sensenova_b200.attention import AttentionModule
+    from oracle.attention import sdpa_window_reference
+    gen = torch.Generator().manual_seed(S + 7)
+    q, k, v = (torch.randn(1, S, H * 128, generator=gen).bfloat16() for _ in range(3))
+    o = AttentionModule(H)(q.cuda(), k.cuda(), v.cuda(), window_size=window)
+    torch.cuda.synchronize()
+    ref = sdpa_window_reference(q, k, v, H, window)
+    assert torch.isfinite(o.float()).all()
+    assert cos(o.cpu(), ref) >= COS
+    # the window changes the result (it is not ignored)
+    if window != (-1, -1) and min(window) >= 0:
+        assert cos(o.cpu(), sdpa_reference(q, k, v, H)) < 0.99
+
+
+def test_attn_fp8_dilated_window_like_reference_self_attention():
+    """SelfAttention with dilated_length d > 1 rearranges b (n d l) c -> (b d) (n l) c before
+    a windowed call with window (L*w, L*w) (kairos_dit.py:452-495); the same here."""
+    from einops import rearrange
+    from kairos_sensenova_b200.attention import AttentionModule
+    from oracle.attention import sdpa_window_reference
+    H, d, L, w, n = 2, 2, 16, 3, 40
+    gen = torch.Generator().manual_seed(11)
+    q, k, v = (torch.randn(1, n * d * L, H * 128, generator=gen).bfloat16() for _ in range(3))
+    r = lambda x: rearrange(x, 'b (n d l) c -> (b d) (n l) c', l=L, d=d)  # noqa: E731
+    qd, kd, vd = r(q), r(k), r(v)
+    o = AttentionModule(H)(qd.cuda(), kd.cuda(), vd.cuda(), window_size=(L * w, L * w))
+    ref = sdpa_window_reference(qd, kd, vd, H, (L * w, L * w))
+    assert cos(o.cpu(), ref) >= COS

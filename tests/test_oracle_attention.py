@@ -41,3 +41,12 @@ def test_residual_term_is_the_e4m3_rounding_error():
     one, s = quant_e4m3(x, 2)
     two, _ = quant_e4m3(x, 2, two_term=True)
     assert (two - x).abs().max() < (one - x).abs().max() / 4
+
+
+def test_window_reference_unbounded_is_full_attention():
+    from oracle.attention import sdpa_window_reference
+    g = torch.Generator().manual_seed(3)
+    q, k, v = (torch.randn(1, 40, 32, generator=g) for _ in range(3))
+    assert torch.allclose(sdpa_window_reference(q, k, v, 2, (-1, -1)), sdpa_reference(q, k, v, 2), atol=1e-6)
+    # a zero-width window is the identity on v
+    assert torch.allclose(sdpa_window_reference(q, k, v, 2, (0, 0)), v, atol=1e-6)
