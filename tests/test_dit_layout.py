@@ -63,3 +63,32 @@ def test_oracle_block_matches_reference_dit_block():
     ref = d['out'][0]
     err = float((y - ref).abs().max() / ref.abs().max())
     assert err < 5e-4, err
+
+
+def test_oracle_gdn_block_matches_reference_dit_block():
+    """The GatedDeltaNet branch of the reference's own ``DiTBlock`` run on CPU
+    (fixture from ``tests/golden/make_dit_gdn_golden.py``: the block's single-device
+    walk in T/8 pieces through one FLA Cache, ``kairos_dit.py:857-922``): (a) the
+    one-shot layer oracle on the branch's whole input equals the reference's
+    chunked walk; (b) the DiT oracle's GDN block (modulation, gated residual,
+    cross-attention, FFN around ``oracle.hybrid.gdn_chain``) equals the block output."""
+    from conftest import GOLDEN
+    from oracle import layers as ol
+    from oracle.dit import block_weights_from_reference, dit_block
+    d = torch.load(GOLDEN / 'dit_block_gdn.pt')
+    sd = d['state_dict']
+    gsd = {k[len('gated_delta.'):]: v for k, v in sd.items() if k.startswith('gated_delta.')}
+    H, hd, eps = d['heads'], d['head_dim'], d['eps']
+    one_shot = ol.gated_deltanet_forward(gsd, d['gdn_in'], H, hd, hd, eps, emulate_bf16=False)
+    err = float((one_shot - d['gdn_out']).abs().max() / d['gdn_out'].abs().max())
+    assert err < 1e-4, err
+    b = block_weights_from_reference(sd)
+    b.update({'Wq': gsd['q_proj.weight'], 'Wk': gsd['k_proj.weight'], 'Wv': gsd['v_proj.weight'],
+              'Wa': gsd['a_proj.weight'], 'Wb': gsd['b_proj.weight'], 'Wg': gsd['g_proj.weight'],
+              'Wo': gsd['o_proj.weight'], 'cq': gsd['q_conv1d.weight'][:, 0], 'ck': gsd['k_conv1d.weight'][:, 0],
+              'cv': gsd['v_conv1d.weight'][:, 0], 'A_log': gsd['A_log'], 'dt_bias': gsd['dt_bias'],
+              'o_norm_w': gsd['o_norm.weight']})
+    y = dit_block(b, d['x'][0], d['context'][0], d['t_mod'][0], H, hd, eps, d['grid'], True, 'silu')
+    ref = d['out'][0]
+    err = float((y - ref).abs().max() / ref.abs().max())
+    assert err < 5e-4, err

@@ -151,3 +151,29 @@ def test_gated_deltanet_cache_walk_matches_one_shot(pieces):
     with torch.no_grad():
         o0, _, none = layer(x)
     assert none is None and torch.equal(o0, full)
+
+
+def test_reference_dit_block_gdn_walk_through_drop_in():
+    """The reference ``DiTBlock``'s own GDN walk (fixture from
+    ``tests/golden/make_dit_gdn_golden.py``: the modulated input in 8 pieces through
+    one FLA Cache, ``kairos_dit.py:857-922``) replayed through the drop-in
+    ``layers.GatedDeltaNet`` + ``layers.Cache`` on the GPU in bf16: the gathered
+    output matches the reference's within 2e-2 max-relative."""
+    from conftest import GOLDEN
+    from kairos_sensenova_b200.layers import Cache, GatedDeltaNet
+    d = torch.load(GOLDEN / 'dit_block_gdn.pt')
+    gsd = {k[len('gated_delta.'):]: v for k, v in d['state_dict'].items() if k.startswith('gated_delta.')}
+    layer = GatedDeltaNet(hidden_size=d['dim'], expand_v=1, head_dim=d['head_dim'], num_heads=d['heads'],
+                          mode='chunk', use_gate=True, norm_eps=d['eps'], layer_idx=0)
+    layer.load_state_dict(gsd)
+    layer = layer.cuda().to(torch.bfloat16)
+    x = d['gdn_in'].cuda().bfloat16()
+    T, n = x.shape[1], d['pieces']
+    cache = Cache.from_legacy_cache()
+    outs = []
+    with torch.no_grad():
+        for s in range(0, T, T // n):
+            o, _, cache = layer(x[:, s:s + T // n].contiguous(), past_key_values=cache, use_cache=True)
+            outs.append(o)
+    got = torch.cat(outs, 1).float().cpu()
+    assert max_rel(got, d['gdn_out']) < 2e-2
