@@ -119,12 +119,12 @@ KB_DEVI float bf(uint32_t u, int hi) { return hi ? __uint_as_float(u & 0xffff000
 // ===========================================================================
 template <int V>
 struct PrepLayout {
-  static constexpr uint32_t KT = 0;            // k tile, then beta e^g k      [2 atoms][64][128 B]
+  static constexpr uint32_t KT = 0;            // k tile                       [2 atoms][64][128 B]
   static constexpr uint32_t QT = 16384;        // q tile; then T1: Lo^T, E (fp32); then the bf16 Ai^T tile
-  static constexpr uint32_t T2 = 32768;        // D^T rows (fp32)
+  static constexpr uint32_t T2 = 32768;        // D^T rows (fp32), then the beta-scaled bf16 Ai^T tile
   static constexpr uint32_t T3 = 49152;        // A (fp32 [64][64], column-swizzled), then M rows
   static constexpr uint32_t T4 = 65536;        // D rows, then M^T rows, then (M^2)^T rows (fp32)
-  static constexpr uint32_t VT = 81920;        // v tile, then beta v           [V/64 atoms][64][128 B]
+  static constexpr uint32_t VT = 81920;        // v tile                        [V/64 atoms][64][128 B]
   static constexpr uint32_t AQS = VT + V * 128;  // staging of the Aqk blob for its bulk store
   static constexpr uint32_t MISC = AQS + 8192;
   static constexpr uint32_t BYTES = MISC + 640 + 1024;
@@ -195,6 +195,7 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_tc_kernel(const __grid_consta
   const uint64_t d_t4 = tc::sdesc_sw128_kmajor(sm + LY::T4);
   const uint64_t d_ai_mn = tc::sdesc_sw128_mnmajor(sm + LY::QT, 8192), d_kt_mn = tc::sdesc_sw128_mnmajor(sm + LY::KT, 8192);
   const uint64_t d_vt_mn = tc::sdesc_sw128_mnmajor(sm + LY::VT, 8192);
+  const uint64_t d_t2_mn = tc::sdesc_sw128_mnmajor(sm + LY::T2, 8192);   // the beta-scaled Ai^T (u product)
   const uint32_t tq = tmem + ((uint32_t)(warp * 32) << 16);     // this warp's TMEM lane quarter
   const int r = warp * 16 + (lane & 15);                          // row of M = 64 products
   const int hc = lane >> 4;                                       // column half
@@ -482,53 +483,25 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_tc_kernel(const __grid_consta
   if (ok) mma_wait();
   PTRACE(7);
   if (ok) {
-    // (I + A)^-1 transposed, half-row r = E + F -> bf16 Ai^T tile (one 64-column atom at QT)
+    // (I + A)^-1 transposed, half-row r = E + F.  The gates of the w / u products scale
+    // the rows of the key / value operands (w = Ai diag(beta e^g) K, u = Ai diag(beta) V,
+    // wy_fast.py:67,77-79); they are applied to the columns of Ai instead, i.e. to the
+    // rows of Ai^T held here: two bf16 tiles, Ai^T diag-scaled by beta e^g (QT, the w
+    // product) and by beta (T2, the u product), and the K and V tiles stay as loaded.
     float f[32];
     ld_half(128, f);
+    const float sw = ms.bs[r] * __expf(ms.gcs[r]), su = ms.bs[r];
 #pragma unroll
     for (int c8 = 0; c8 < 4; ++c8) {
-      uint32_t w[4];
+      uint32_t ww[4], wu[4];
 #pragma unroll
-      for (int q = 0; q < 4; ++q)
-        w[q] = pack_bf16(e[8 * c8 + 2 * q] + f[8 * c8 + 2 * q], e[8 * c8 + 2 * q + 1] + f[8 * c8 + 2 * q + 1]);
-      *reinterpret_cast<uint4*>(sm + LY::QT + swz(r, 4 * hc + c8)) = make_uint4(w[0], w[1], w[2], w[3]);
-    }
-    // k rows -> bf16(bf16(k beta) e^g) (wy_fast.py:77-79), v rows -> bf16(v beta) (:67), in
-    // place; each thread loads its 8 chunks of a row first, then converts and stores them
-    // (the loads do not wait behind the stores)
-    {
-      const int rr = tid & 63, a = tid >> 6;
-      const float b = ms.bs[rr], eg = __expf(ms.gcs[rr]);
-      unsigned char* row = sm + LY::KT + a * 8192;
-      uint4 v4[8];
-#pragma unroll
-      for (int ch = 0; ch < 8; ++ch) v4[ch] = *reinterpret_cast<const uint4*>(row + swz(rr, ch));
-#pragma unroll
-      for (int ch = 0; ch < 8; ++ch) {
-        uint32_t* w = reinterpret_cast<uint32_t*>(&v4[ch]);
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-          w[q] = pack_bf16(bf16_round(bf(w[q], 0) * b) * eg, bf16_round(bf(w[q], 1) * b) * eg);
+      for (int q = 0; q < 4; ++q) {
+        const float a0 = e[8 * c8 + 2 * q] + f[8 * c8 + 2 * q], a1 = e[8 * c8 + 2 * q + 1] + f[8 * c8 + 2 * q + 1];
+        ww[q] = pack_bf16(a0 * sw, a1 * sw);
+        wu[q] = pack_bf16(a0 * su, a1 * su);
       }
-#pragma unroll
-      for (int ch = 0; ch < 8; ++ch) *reinterpret_cast<uint4*>(row + swz(rr, ch)) = v4[ch];
-    }
-#pragma unroll 1
-    for (int job = tid; job < 64 * (V / 64); job += 128) {
-      const int rr = job & 63, a = job >> 6;
-      const float b = ms.bs[rr];
-      unsigned char* row = sm + LY::VT + a * 8192;
-      uint4 v4[8];
-#pragma unroll
-      for (int ch = 0; ch < 8; ++ch) v4[ch] = *reinterpret_cast<const uint4*>(row + swz(rr, ch));
-#pragma unroll
-      for (int ch = 0; ch < 8; ++ch) {
-        uint32_t* w = reinterpret_cast<uint32_t*>(&v4[ch]);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) w[q] = pack_bf16(bf(w[q], 0) * b, bf(w[q], 1) * b);
-      }
-#pragma unroll
-      for (int ch = 0; ch < 8; ++ch) *reinterpret_cast<uint4*>(row + swz(rr, ch)) = v4[ch];
+      *reinterpret_cast<uint4*>(sm + LY::QT + swz(r, 4 * hc + c8)) = make_uint4(ww[0], ww[1], ww[2], ww[3]);
+      *reinterpret_cast<uint4*>(sm + LY::T2 + swz(r, 4 * hc + c8)) = make_uint4(wu[0], wu[1], wu[2], wu[3]);
     }
   }
   tc::fence_proxy_async_smem();
@@ -547,7 +520,7 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_tc_kernel(const __grid_consta
     for (int vs = 0; vs < V / 128; ++vs) {
       const uint64_t dv = d_vt_mn + (uint64_t)(vs * 16384 / 16);
 #pragma unroll
-      for (int ks = 0; ks < 4; ++ks) tc::mma_bf16(tmem + 128 + 64 * vs, dv + ks * 128, dai + ks * 128, ID_U, ks > 0);
+      for (int ks = 0; ks < 4; ++ks) tc::mma_bf16(tmem + 128 + 64 * vs, dv + ks * 128, d_t2_mn + ks * 128, ID_U, ks > 0);
     }
     tc::tc_commit(&ms.mma_bar);
   }
