@@ -331,6 +331,7 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_tc_kernel(const __grid_consta
       gj[4 * i] = g4.x; gj[4 * i + 1] = g4.y; gj[4 * i + 2] = g4.z; gj[4 * i + 3] = g4.w;
     }
     tc::tmem_wait_ld();
+    PTRACE(23);
 #pragma unroll
     for (int c8 = 0; c8 < 4; ++c8) {
       uint32_t w[4];
@@ -350,9 +351,11 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_tc_kernel(const __grid_consta
       *reinterpret_cast<uint4*>(sm + LY::AQS + swz(r, 4 * hc + c8)) = make_uint4(w[0], w[1], w[2], w[3]);
     }
   }
+  PTRACE(24);
   tc::fence_proxy_async_smem();
   // the q tile is overwritten next: the TMA store of the normalised q / k must have read it
   if (tid == 0) tc::bulk_wait_group_read0();
+  PTRACE(25);
   __syncthreads();
   if (ok && tid == 0) {
     tc::bulk_store(reinterpret_cast<unsigned char*>(p.ab) + ((size_t)c * H + h) * AQK_BYTES, sm + LY::AQS, AQK_BYTES);
@@ -374,6 +377,7 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_tc_kernel(const __grid_consta
       }
       st_f32x8(t1, r, 4 * hc + c8, v8);
     }
+    PTRACE(20);
     // thread t < 64: column t % 16 of block t / 16's inverse (row t of D^T);
     // thread t >= 64: row (t - 64) % 16 of it (row t - 64 of D)
     const int rr = tid & 63, b = rr >> 4, cc = rr & 15;
@@ -397,6 +401,7 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_tc_kernel(const __grid_consta
         if (j < cc) x[j] = -acc;
       }
     }
+    PTRACE(21);
     unsigned char* dst = sm + (tid < 64 ? LY::T2 : LY::T4);
 #pragma unroll
     for (int c8 = 0; c8 < 8; ++c8) {
@@ -405,6 +410,7 @@ __global__ void __launch_bounds__(128, 2) gdn_prep_tc_kernel(const __grid_consta
       for (int e = 0; e < 8; ++e) v8[e] = ((c8 >> 1) == b) ? x[(c8 & 1) * 8 + e] : 0.f;
       st_f32x8(dst, rr, c8, v8);
     }
+    PTRACE(22);
   }
   tc::fence_proxy_async_smem();
   __syncthreads();
