@@ -754,7 +754,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_tc_kernel(const __gri
       const uint64_t dw0 = tc::sdesc_sw128_kmajor(sm + LY::W), dq0 = tc::sdesc_sw128_kmajor(sm + LY::Q);
       const uint64_t dk0 = tc::sdesc_sw128_mnmajor(sm + LY::K, 8192), da0 = tc::sdesc_sw128_kmajor(sm + LY::A);
       auto wait_all = [&](uint64_t* bar, uint32_t parity) {
-        return __all_sync(0xffffffffu, tc::mbar_test_wait_loop(bar, parity, WAIT_BUDGET));
+        return __all_sync(0xffffffffu, wait_(bar, parity));
       };
       bool ok = true;
       for (int li = 0; li < nl && ok; ++li) {
@@ -765,6 +765,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_tc_kernel(const __gri
              (!out || li < 2 || wait_all(&ms.o_free[b], ((li >> 1) - 1) & 1)) && !aborted();
         if (!ok) { if (leader) fail(p.err, 81); break; }
         tc::tc_fence_after();
+        if (lane == 0) STRACE(li, 6);
         if (leader) {
 #pragma unroll
           for (int ks = 0; ks < 8; ++ks)
