@@ -627,6 +627,7 @@ struct StMisc {
   uint32_t tmem_base;
   int abort;
   int keep_tmem;
+  int err_seen;                    // the error word as thread 0 read it at entry
 };
 
 // The output tile of one chunk into the staging tile: thread v (TMEM lane v) writes
@@ -691,13 +692,23 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_tc_kernel(const __gri
   unsigned char* sm = align1024(smem_raw);
   StMisc& ms = *reinterpret_cast<StMisc*>(sm + LY::MISC);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, H = p.H;
+  // the 1024-byte alignment of the dynamic shared memory must leave room for the
+  // control block (it runs into the alignment slack); otherwise report and stop
+  if ((uint32_t)(sm - smem_raw) + LY::MISC + (uint32_t)sizeof(StMisc) > LY::BYTES) {
+    if (tid == 0) fail(p.err, 73);
+    return;
+  }
   const int nseg = p.seg_mode ? p.nseg : 1;
   GTR_INIT;
   const int nh = blockIdx.y / nseg, seg = blockIdx.y % nseg, n = nh / H, h = nh % H;
   const bool trans = p.seg_mode == 1 && (int)blockIdx.x >= V / 128;
   const int v0 = trans ? 0 : blockIdx.x * 128;
   if (p.seg_mode == 1 && (seg == nseg - 1 || (trans && seg == 0))) return;
-  if (*reinterpret_cast<volatile int*>(p.err)) return;   // an earlier kernel or CTA already gave up
+  // an earlier kernel or CTA already gave up: the whole CTA leaves together (one read,
+  // shared), since the state and output warps later meet at named barriers
+  if (tid == 0) ms.err_seen = *reinterpret_cast<volatile int*>(p.err);
+  __syncthreads();
+  if (ms.err_seen) return;
   int bos, Tn, cbase;
   if (p.cu_seqlens) {
     bos = p.cu_seqlens[n];
@@ -882,8 +893,9 @@ __global__ void __launch_bounds__(ST_THREADS, 1) gdn_state_tc_kernel(const __gri
     };
       for (int lo = 0; lo < nl; ++lo) {
         const bool w = wait_(&ms.o_full[lo & 1], (lo >> 1) & 1);
-        if (!__all_sync(0xffffffffu, w)) {
-          if (lane == 0) fail(p.err, 61);
+        // the four output warps decide together (they meet at named barrier 2 in emit)
+        if (!tc::bar_red_and(2, 128, w)) {
+          if (tid == 256) fail(p.err, 61);
           ms.abort = 1;
           break;
         }
