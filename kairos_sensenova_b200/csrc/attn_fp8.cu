@@ -72,7 +72,9 @@ KB_DEVI uint32_t quant8(const __nv_bfloat16* e, float r, int j0) {
 
 template <int D>
 __global__ void __launch_bounds__(256) attn_quant_kernel(Params p) {
-  constexpr int LDT = 64 + 8;   // bf16 elements per V^T row in shared memory (padded)
+  // bf16 elements per V^T row in shared memory: padded by 2, so the 16 lanes that hold
+  // 8-channel groups of one token (channels 8 apart) store into 4 banks, not one
+  constexpr int LDT = 64 + 2;
   __shared__ __align__(16) __nv_bfloat16 vts[D * LDT];
   __shared__ int kmax;          // max key norm of this 64-token tile (float bits, >= 0)
   const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H, H = p.H;
@@ -122,8 +124,10 @@ __global__ void __launch_bounds__(256) attn_quant_kernel(Params p) {
   // write the V^T tile: D rows x 64 tokens (128 bytes per row)
   for (int idx = threadIdx.x; idx < D * 8; idx += blockDim.x) {
     const int d = idx >> 3, seg = (idx & 7) * 8;
+    // (rows are 4-byte aligned: four 32-bit reads)
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(&vts[d * LDT + seg]);
     *reinterpret_cast<uint4*>(p.vt + ((size_t)bh * D + d) * p.S_pad + t0 + seg) =
-        *reinterpret_cast<const uint4*>(&vts[d * LDT + seg]);
+        make_uint4(src[0], src[1], src[2], src[3]);
   }
 }
 
